@@ -1,0 +1,452 @@
+"""Benchmark of the fused RMSNorm + RoPE path, forward + backward.
+
+One step = one training-style pass of the path over one batch: the hidden-state
+RMSNorm forward (``bloth_b200.rms_norm``), the q/k per-head RMSNorm + RoPE
+forward (``bloth_b200.fused_qk_norm_rope``, cos/sin from positions
+in-register), then the backward of both for given output gradients (dx,
+dweight, dq, dk, dwq, dwk) via ``torch.autograd.grad``.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+                    [--impl b200|reference] [--scaling weak|strong]
+
+N > 1 is launched with torch.distributed.run, one rank per GPU; every rank
+processes its own shard of token rows (no collective on the data path); the
+step time is the max over ranks. Prints one JSON line on rank 0.
+
+``--impl reference`` times the reference's CPU path instead: the oracle's
+PyTorch restatement in float32 on all host cores, on a bounded sample of the
+same workload per step (the reference has no CPU implementation of its own).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "fused RMSNorm+RoPE fwd+bwd tokens/s and HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+NOMINAL_HBM_GBS = 8000.0
+
+# name -> (batch, seq, hidden (0 = none), heads_q, heads_kv, head_dim, theta, eps, packed)
+WORKLOADS = {
+    "llama3-8b": (8, 4096, 4096, 32, 8, 128, 5e5, 1e-5, False),
+    "llama3.2-1b": (4, 2048, 2048, 32, 8, 64, 5e5, 1e-5, False),
+    "qwen3-8b-packed": (16, 8192, 0, 32, 8, 128, 1e6, 1e-6, True),
+}
+
+
+def describe(name: str) -> str:
+    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+    parts = []
+    if Hd:
+        parts.append(f"hidden [{B},{S},{Hd}] RMSNorm")
+    parts.append(f"q [{B},{S},{Hq},{D}] + k [{B},{S},{Hk},{D}] norm+RoPE")
+    extra = ", packed documents (lengths U[64,2048])" if packed else ""
+    return f"{name}: " + " + ".join(parts) + f", bf16, theta {theta:g}, eps {eps:g}{extra}"
+
+
+def step_bytes(tokens: int, name: str, elem: int = 2) -> dict:
+    """Algorithmic HBM bytes of one fwd+bwd step over `tokens` tokens.
+
+    Per normalised row of width W: forward reads x and writes y (2*W*s) and
+    writes rstd (4 B); backward reads dy and x and writes dx (3*W*s) and reads
+    rstd (4 B). Positions are int64: 8 B per token per pass. Weights and
+    dweight (a few KB) are not counted.
+    """
+    _, _, Hd, Hq, Hk, D, _, _, _ = WORKLOADS[name]
+    rows = Hq + Hk
+    out = {
+        "rms_fwd": tokens * (2 * Hd * elem + 4) if Hd else 0,
+        "rms_bwd": tokens * (3 * Hd * elem + 4) if Hd else 0,
+        "qk_fwd": tokens * (rows * (2 * D * elem + 4) + 8),
+        "qk_bwd": tokens * (rows * (3 * D * elem + 4) + 8),
+    }
+    out["total"] = sum(out.values())
+    return out
+
+
+# ------------------------------------------------------------- inputs
+def make_inputs(name: str, tokens_b: int, dev, seed: int, shard=(0, 1)):
+    """Seeded synthetic inputs on `dev` for batch rows shard[0]::shard[1]."""
+    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+    g = torch.Generator(device=dev).manual_seed(seed)
+    bf = torch.bfloat16
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).to(bf)
+
+    def weight(n):
+        return (1 + 0.1 * torch.randn(n, generator=g, device=dev)).to(bf)
+
+    b = tokens_b
+    inp = {}
+    if Hd:
+        inp["x"] = randn(b, S, Hd)
+        inp["w"] = weight(Hd)
+        inp["gy"] = randn(b, S, Hd)
+    inp["q"] = randn(b, S, Hq, D)
+    inp["k"] = randn(b, S, Hk, D)
+    inp["wq"] = weight(D)
+    inp["wk"] = weight(D)
+    inp["gq"] = randn(b, S, Hq, D)
+    inp["gk"] = randn(b, S, Hk, D)
+    if packed:
+        from oracle.reference_path import packed_position_ids  # seeded document layout
+        pos = packed_position_ids(b, S, 64, 2048, torch.Generator().manual_seed(seed + shard[0]))
+        inp["pos"] = pos.to(dev)
+    else:
+        inp["pos"] = torch.arange(S, device=dev, dtype=torch.int64).expand(b, S).contiguous()
+    half = D // 2
+    inp["inv_freq"] = (1.0 / (theta ** (torch.arange(0, half, dtype=torch.float32) / half))).to(dev)
+    inp["eps"] = eps
+    return inp
+
+
+def run_step(inp, bloth):
+    """One fwd+bwd pass through the public API; returns the gradients."""
+    leaves = []
+    outs, grads = [], []
+    if "x" in inp:
+        x = inp["x"].requires_grad_(True)
+        w = inp["w"].requires_grad_(True)
+        outs.append(bloth.rms_norm(x, w, inp["eps"]))
+        grads.append(inp["gy"])
+        leaves += [x, w]
+    q = inp["q"].requires_grad_(True)
+    k = inp["k"].requires_grad_(True)
+    wq = inp["wq"].requires_grad_(True)
+    wk = inp["wk"].requires_grad_(True)
+    qo, ko = bloth.fused_qk_norm_rope(q, k, wq, wk, inp["pos"], inp["inv_freq"], inp["eps"])
+    outs += [qo, ko]
+    grads += [inp["gq"], inp["gk"]]
+    leaves += [q, k, wq, wk]
+    res = torch.autograd.grad(outs, leaves, grads)
+    return outs, res
+
+
+# ------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f".clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
+                stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as fh:
+            for line in fh:
+                f = [c.strip() for c in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx = float(f[2])
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------- CPU arm
+def cpu_port_step(name: str, tokens: int, seed: int = 0):
+    """The oracle (float32, the reference golden's precision) fwd+bwd over
+    `tokens` tokens of the workload; returns a callable running one step."""
+    import oracle
+    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+    g = torch.Generator().manual_seed(seed)
+    bf = torch.bfloat16
+    t = tokens
+    x = torch.randn(t, Hd, generator=g).to(bf) if Hd else None
+    w = (1 + 0.1 * torch.randn(Hd, generator=g)).to(bf) if Hd else None
+    gy = torch.randn(t, Hd, generator=g).to(bf) if Hd else None
+    q = torch.randn(1, t, Hq, D, generator=g).to(bf)
+    k = torch.randn(1, t, Hk, D, generator=g).to(bf)
+    wq = (1 + 0.1 * torch.randn(D, generator=g)).to(bf)
+    wk = (1 + 0.1 * torch.randn(D, generator=g)).to(bf)
+    gq = torch.randn(1, t, Hq, D, generator=g).to(bf)
+    gk = torch.randn(1, t, Hk, D, generator=g).to(bf)
+    pos = torch.arange(t) % S
+    inv = oracle.inv_freq(D, theta)
+    f32 = torch.float32
+
+    def step():
+        if Hd:
+            oracle.rms_norm_fwd_bwd(x, w, gy, eps, compute=f32)
+        oracle.qk_norm_rope_fwd_bwd(q, k, wq, wk, gq, gk, pos.view(1, t), inv, eps, compute=f32)
+
+    return step
+
+
+def time_cpu(name: str, budget_s: float, steps: int | None = None, warmup: int = 1):
+    """Times the oracle port on all host cores; returns (tokens/s, sample, cores).
+
+    Without `steps`, runs 512-token steps for `budget_s` seconds. With `steps`,
+    the tokens per step are scaled down (to >= 16) so that all steps take
+    about `budget_s` seconds.
+    """
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    tokens = 512
+    step = cpu_port_step(name, tokens)
+    t0 = time.perf_counter()
+    step()
+    one = time.perf_counter() - t0
+    if steps is not None:
+        while tokens > 16 and one * steps > budget_s:
+            tokens //= 2
+            one /= 2
+        step = cpu_port_step(name, tokens)
+    for _ in range(warmup):
+        step()
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        step()
+        n += 1
+        el = time.perf_counter() - t0
+        if (steps is not None and n >= steps) or (steps is None and el >= budget_s):
+            break
+    return tokens * n / el, f"{tokens} tokens of the workload per step, {n} steps, {el:.1f} s", cores
+
+
+# ------------------------------------------------------------- main
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--workload", default="llama3-8b", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    name = args.workload
+    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        tps, sample, cores = time_cpu(name, 90.0, steps=max(args.steps, 1),
+                                     warmup=min(max(args.warmup, 0), 3))
+        line = {"metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
+                "steps": args.steps, "warmup": args.warmup, "impl": "reference",
+                "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": describe(name), "device": "cpu"},
+                "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores,
+                                 "kind": "port", "sample": sample},
+                "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import bloth_b200 as bloth
+    from bloth_b200 import _lib
+
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py: no CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+
+    # tokens this rank processes per step
+    if args.scaling == "weak":
+        b_local = B
+    else:
+        if B % world:
+            raise SystemExit(f"strong scaling needs batch {B} divisible by {world}")
+        b_local = B // world
+    tokens_local = b_local * S
+    inp = make_inputs(name, b_local, dev, seed=1234 + rank, shard=(rank, world))
+    nbytes = step_bytes(tokens_local, name)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        run_step(inp, bloth)
+    barrier()
+
+    # ---- device-resident timed region, per-launch events for the roofline
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk, _lib.timing_launches() as timer:
+        barrier()
+        start.record()
+        for _ in range(args.steps):
+            run_step(inp, bloth)
+        end.record()
+        barrier()
+    ms = start.elapsed_time(end)
+    per_kernel = timer.summary()
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    tokens_total = tokens_local * world
+    value = tokens_total / (ms_step / 1e3)
+    gbps = nbytes["total"] * world / (ms_step / 1e3) / 1e9
+
+    # kernels launched per C-ABI call: backward entry points add the dweight reduce
+    launches = sum(v["launches"] * (2 if k.endswith("_bwd") else 1) for k, v in per_kernel.items())
+    kb = {"bloth_rmsnorm_fwd": "rms_fwd", "bloth_rmsnorm_bwd": "rms_bwd",
+          "bloth_qk_norm_rope_fwd": "qk_fwd", "bloth_qk_norm_rope_bwd": "qk_bwd"}
+    top = max(per_kernel.items(), key=lambda kv: kv[1]["total_ms"])
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            peaks = json.load(fh)
+    except OSError:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    top_bytes = nbytes[kb[top[0]]]
+    achieved = top_bytes / (top[1]["mean_ms"] / 1e3) / 1e9
+    kernels = {k: {"launches": v["launches"], "mean_us": round(v["mean_ms"] * 1e3, 2),
+                   "gbps": round(nbytes[kb[k]] / (v["mean_ms"] / 1e3) / 1e9, 1)}
+               for k, v in per_kernel.items()}
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if args.e2e_steps > 0:
+        e2e = end_to_end(inp, bloth, dev, args.e2e_steps, barrier, dist, tokens_total)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        tps, sample, cores = time_cpu(name, args.cpu_seconds)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": sample}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": describe(name), "tokens_per_gpu": tokens_local,
+                       "parallelism": f"{world} independent row shards, no collective",
+                       "l2": "inputs larger than L2 (each tensor >= 67 MB at this size), no flush",
+                       "step_gb_per_gpu": round(nbytes["total"] / 1e9, 4),
+                       "gbps": round(gbps, 1),
+                       "frac_of_8tbs_per_gpu": round(gbps / world / NOMINAL_HBM_GBS, 4),
+                       "frac_of_measured_per_gpu": round(gbps / world / peak, 4),
+                       "kernels": kernels},
+            "roofline": {"bound": "hbm", "kernel": top[0], "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
+                         if "hbm_gbs" in peaks else "fallback 6650 GB/s",
+                         "traffic": None},
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
+    """Same step through the public API with the inputs in pinned host memory:
+    every step copies its inputs host->device and all of its results
+    (outputs and gradients) device->host inside the timed region."""
+    keys_in = [k for k in ("x", "gy", "q", "k", "gq", "gk", "pos") if k in inp]
+    host = {k: inp[k].detach().cpu().pin_memory() for k in keys_in}
+    small = {k: v for k, v in inp.items() if k not in keys_in}
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    outs_host = None
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def one():
+        nonlocal outs_host
+        d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+        d.update(small)
+        outs, grads = run_step(d, bloth)
+        res = [t.detach() for t in list(outs) + list(grads)]
+        if outs_host is None:
+            outs_host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in res]
+        for h, t in zip(outs_host, res):
+            h.copy_(t, non_blocking=True)
+
+    one()
+    barrier()
+    start.record()
+    for _ in range(steps):
+        one()
+    end.record()
+    barrier()
+    ms = start.elapsed_time(end)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    d2h = sum(t.numel() * t.element_size() for t in outs_host)
+    return {"value": tokens_total / (ms / steps / 1e3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms / steps}
+
+
+if __name__ == "__main__":
+    main()

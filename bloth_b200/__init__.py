@@ -1,0 +1,48 @@
+"""bloth_b200 - B200 (sm_100a) kernels for Bloth's fused RMSNorm + RoPE path.
+
+Drop-in for the reference's names on this path (bloth/bloth/__init__.py:18-42
+and kernels/__init__.py:7-8):
+
+    rms_norm, BlothRMSNorm, fused_norm_qkv, BlothFusedNormQKV, rope_embedding,
+    BlothRoPE, patch_model, FastModel, kernels.rms_norm, kernels.bloth_rms_norm,
+    kernels.fused_norm_rope, kernels.rope_embedding
+
+plus fused_qk_norm_rope / BlothQKNormRoPE (q and k per-head norm + RoPE in one
+launch, cos/sin from positions in-register). The compute runs in hand-written
+CUDA behind the C ABI of include/bloth_b200.h; importing this package does not
+touch the GPU, and every op raises if the library or a CUDA device is missing.
+"""
+from __future__ import annotations
+
+__version__ = "0.1.0"
+
+from . import kernels  # noqa: F401
+from .kernels import fused_norm_rope, fused_qk_norm_rope, apply_rope  # noqa: F401
+from .modules import (  # noqa: F401
+    BlothFusedNormQKV,
+    BlothQKNormRoPE,
+    BlothRMSNorm,
+    BlothRoPE,
+    fused_norm_qkv,
+    rms_norm,
+    rope_inv_freq,
+)
+from .kernels.rope import rope_embedding  # noqa: F401
+from .patch import FastModel, patch_model  # noqa: F401
+
+__all__ = [
+    "kernels",
+    "rms_norm",
+    "BlothRMSNorm",
+    "fused_norm_qkv",
+    "BlothFusedNormQKV",
+    "fused_norm_rope",
+    "fused_qk_norm_rope",
+    "BlothQKNormRoPE",
+    "rope_embedding",
+    "apply_rope",
+    "BlothRoPE",
+    "rope_inv_freq",
+    "patch_model",
+    "FastModel",
+]

@@ -1,0 +1,188 @@
+"""ctypes binding of ``libbloth_b200.so`` (the C ABI in include/bloth_b200.h).
+
+The library is loaded on first use. There is no fallback: if the shared
+library is missing, or a tensor is not on a CUDA device, the call raises.
+Launches go to the current torch CUDA stream of the tensors' device; outputs
+and workspaces are allocated by the callers through torch's caching
+allocator, never inside the library.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from contextlib import contextmanager
+
+import torch
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libbloth_b200.so")
+
+F32, BF16, F16, I32, I64 = 0, 1, 2, 3, 4
+ERR_ALIGN = 3
+
+_DTYPE_CODE = {
+    torch.float32: F32,
+    torch.bfloat16: BF16,
+    torch.float16: F16,
+    torch.int32: I32,
+    torch.int64: I64,
+}
+
+_lib = None
+_lock = threading.Lock()
+
+_vp = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_int = ctypes.c_int
+_f32 = ctypes.c_float
+_sz = ctypes.c_size_t
+_i64p = ctypes.POINTER(ctypes.c_int64)
+
+_SIGNATURES = {
+    "bloth_version": (_int, []),
+    "bloth_strerror": (ctypes.c_char_p, [_int]),
+    "bloth_last_cuda_error": (_int, []),
+    "bloth_rmsnorm_fwd": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _f32, _int, _int, _vp]),
+    "bloth_rmsnorm_bwd_workspace_bytes": (_sz, [_i64, _i64, _int]),
+    "bloth_rmsnorm_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int,
+                                 _int, _vp, _sz, _vp]),
+    "bloth_norm_rope_fwd": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _int, _i64, _vp, _i64, _vp,
+                                   _i64, _i64, _f32, _int, _int, _vp]),
+    "bloth_norm_rope_bwd_workspace_bytes": (_sz, [_i64, _i64, _int]),
+    "bloth_norm_rope_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _int, _i64, _vp, _vp,
+                                   _i64, _vp, _i64, _i64, _int, _int, _vp, _sz, _vp]),
+    "bloth_qk_norm_rope_fwd": (_int, [_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
+                                      _vp, _vp, _vp, _i64p, _int, _vp, _vp, _vp, _i64p, _int,
+                                      _i64, _i64, _i64, _i64, _i64, _f32, _int, _int, _vp]),
+    "bloth_qk_norm_rope_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _int]),
+    "bloth_qk_norm_rope_bwd": (_int, [_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
+                                      _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p,
+                                      _int, _vp, _vp, _vp, _i64p, _int, _i64, _i64, _i64, _i64,
+                                      _i64, _int, _int, _vp, _sz, _vp]),
+    "bloth_rope": (_int, [_vp, _i64p, _vp, _i64p, _vp, _i64p, _int, _vp, _vp, _vp, _i64p, _int,
+                          _i64, _i64, _i64, _i64, _int, _int, _vp]),
+}
+
+
+def load() -> ctypes.CDLL:
+    """Loads the shared library (once) and declares every entry point."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"[Bloth] CUDA extension {LIB_PATH} is not built; run "
+                    "`python -m bloth_b200.build` (nvcc, sm_100a)")
+            lib = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise TypeError(f"[Bloth] unsupported dtype {dt}") from None
+
+
+class BlothError(RuntimeError):
+    """A status code returned by the C ABI."""
+
+    def __init__(self, status: int, what: str):
+        lib = load()
+        msg = lib.bloth_strerror(status).decode()
+        if status == 6:
+            msg += f" (cudaError {lib.bloth_last_cuda_error()})"
+        super().__init__(f"[Bloth] {what}: {msg}")
+        self.status = status
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        raise BlothError(status, what)
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    """The reference's convention (fused_norm_qkv_rope.py:133): CUDA tensors only."""
+    for t in tensors:
+        if t is not None:
+            assert t.is_cuda, "[Bloth] CUDA GPU required"
+
+
+def ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def strides(vals) -> ctypes.Array:
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+
+
+def stream_of(t: torch.Tensor) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def aligned16(t: torch.Tensor) -> torch.Tensor:
+    """t itself when its data is 16-byte aligned, else an aligned copy."""
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
+# ------------------------------------------------------------- launch timer
+class LaunchTimer:
+    """Records a CUDA event pair around every C-ABI launch, on the launching
+    stream, grouped by entry point. Used by bench.py to time individual
+    kernels inside its timed region."""
+
+    def __init__(self):
+        self.pairs: dict[str, list] = {}
+
+    def wrap(self, name: str, t: torch.Tensor, fn):
+        s = torch.cuda.current_stream(t.device)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        rc = fn()
+        b.record(s)
+        self.pairs.setdefault(name, []).append((a, b))
+        return rc
+
+    def summary(self) -> dict[str, dict]:
+        out = {}
+        for name, evs in self.pairs.items():
+            ms = [a.elapsed_time(b) for a, b in evs]
+            out[name] = {"launches": len(ms), "total_ms": sum(ms), "mean_ms": sum(ms) / len(ms)}
+        return out
+
+
+_timer: LaunchTimer | None = None
+
+
+@contextmanager
+def timing_launches():
+    global _timer
+    prev, _timer = _timer, LaunchTimer()
+    try:
+        yield _timer
+    finally:
+        _timer = prev
+
+
+def call(name: str, t: torch.Tensor, *args) -> int:
+    """Calls entry point `name` with `t`'s device current (the C ABI launches
+    on the calling thread's current device)."""
+    fn = getattr(load(), name)
+    if t.device.index != torch.cuda.current_device():
+        with torch.cuda.device(t.device):
+            return call(name, t, *args)
+    if _timer is None:
+        return fn(*args)
+    return _timer.wrap(name, t, lambda: fn(*args))

@@ -1,0 +1,163 @@
+// Shared device helpers for the RMSNorm / RoPE kernels: element conversion,
+// 16-byte packed global loads and stores, warp and row-group reductions, and
+// the host-side launch bookkeeping (SM count and occupancy caches).
+//
+// Every kernel in this library is HBM-bound: each element is read once from
+// global memory as part of a 16-byte vector, converted to fp32, reduced with
+// warp shuffles, and written once. Tensor cores are not used.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/bloth_b200.h"
+
+namespace bloth {
+
+// ---------------------------------------------------------------------------
+// element conversion
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+template <> __device__ __forceinline__ __half from_f<__half>(float v) { return __float2half_rn(v); }
+
+template <typename T> struct DTypeOf;
+template <> struct DTypeOf<float> { static constexpr int value = BLOTH_F32; };
+template <> struct DTypeOf<__nv_bfloat16> { static constexpr int value = BLOTH_BF16; };
+template <> struct DTypeOf<__half> { static constexpr int value = BLOTH_F16; };
+
+// Accumulator type of the weight-gradient partial sums: fp64 for fp32 tensors
+// (so that dweight stays within a few fp32 ulps of the exact sum at any row
+// count), fp32 for 16-bit tensors (whose dweight is rounded to 16 bits anyway).
+template <typename T> struct AccOf { using type = float; };
+template <> struct AccOf<float> { using type = double; };
+
+// ---------------------------------------------------------------------------
+// packed global access: VEC elements of T as one aligned access
+// ---------------------------------------------------------------------------
+template <typename T, int VEC>
+struct alignas(sizeof(T) * VEC) Pack {
+  T v[VEC];
+};
+
+template <int NB> struct RawOf;
+template <> struct RawOf<16> { using type = uint4; };
+template <> struct RawOf<8> { using type = uint2; };
+template <> struct RawOf<4> { using type = unsigned int; };
+template <> struct RawOf<2> { using type = unsigned short; };
+
+// Read-only (non-coherent) load of one pack. Inputs are never written by the
+// kernel that reads them, so the read-only path is always legal here.
+template <typename T, int VEC>
+__device__ __forceinline__ Pack<T, VEC> ldg_pack(const T* p) {
+  using R = typename RawOf<sizeof(T) * VEC>::type;
+  R r = __ldg(reinterpret_cast<const R*>(p));
+  Pack<T, VEC> out;
+  memcpy(&out, &r, sizeof(out));
+  return out;
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void stg_pack(T* p, const Pack<T, VEC>& v) {
+  *reinterpret_cast<Pack<T, VEC>*>(p) = v;
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void unpack(const Pack<T, VEC>& pk, float (&f)[VEC]) {
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) f[e] = to_f(pk.v[e]);
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ Pack<T, VEC> pack(const float (&f)[VEC]) {
+  Pack<T, VEC> pk;
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) pk.v[e] = from_f<T>(f[e]);
+  return pk;
+}
+
+// Scalar load of element i of a tensor whose element type is only known at
+// run time (weights, cos/sin tables). The switch is uniform across the grid.
+__device__ __forceinline__ float ld_any(const void* base, int64_t i, int dt) {
+  switch (dt) {
+    case BLOTH_BF16: return __bfloat162float(__ldg(reinterpret_cast<const __nv_bfloat16*>(base) + i));
+    case BLOTH_F16: return __half2float(__ldg(reinterpret_cast<const __half*>(base) + i));
+    default: return __ldg(reinterpret_cast<const float*>(base) + i);
+  }
+}
+
+// VEC consecutive elements starting at element i, runtime element type.
+// `vec_ok` promises that base + i is aligned to VEC * element size, so the
+// load can be issued as packed accesses.
+template <int VEC>
+__device__ __forceinline__ void ld_any_vec(const void* base, int64_t i, int dt, bool vec_ok,
+                                           float (&out)[VEC]) {
+  if (vec_ok) {
+    if (dt == BLOTH_F32) {
+      if constexpr (VEC % 4 == 0) {
+#pragma unroll
+        for (int q = 0; q < VEC / 4; ++q) {
+          float4 v = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(base) + i) + q);
+          out[4 * q + 0] = v.x; out[4 * q + 1] = v.y; out[4 * q + 2] = v.z; out[4 * q + 3] = v.w;
+        }
+        return;
+      }
+    } else if (dt == BLOTH_BF16) {
+      if constexpr (VEC == 8 || VEC == 4) {
+        Pack<__nv_bfloat16, VEC> pk = ldg_pack<__nv_bfloat16, VEC>(reinterpret_cast<const __nv_bfloat16*>(base) + i);
+        unpack(pk, out);
+        return;
+      }
+    } else {
+      if constexpr (VEC == 8 || VEC == 4) {
+        Pack<__half, VEC> pk = ldg_pack<__half, VEC>(reinterpret_cast<const __half*>(base) + i);
+        unpack(pk, out);
+        return;
+      }
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) out[e] = ld_any(base, i + e, dt);
+}
+
+__device__ __forceinline__ void st_any(void* base, int64_t i, int dt, float v) {
+  switch (dt) {
+    case BLOTH_BF16: reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v); break;
+    case BLOTH_F16: reinterpret_cast<__half*>(base)[i] = __float2half_rn(v); break;
+    default: reinterpret_cast<float*>(base)[i] = v; break;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// reductions
+// ---------------------------------------------------------------------------
+// Butterfly sum over aligned groups of WIDTH lanes (WIDTH a power of two
+// <= 32). Every lane of a group ends with the bit-identical total, because
+// each step adds the same two operands in both partner lanes.
+template <int WIDTH>
+__device__ __forceinline__ float group_lane_sum(float v) {
+#pragma unroll
+  for (int o = WIDTH / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// host-side helpers (defined in launch.cu)
+// ---------------------------------------------------------------------------
+int device_sm_count();  // SM count of the current device (cached per device)
+// Resident CTAs per SM for `func` at `block` threads and `smem` dynamic bytes
+// (cached per device and function).
+int occupancy(const void* func, int block, size_t smem);
+// Records `err` as the calling thread's last CUDA error and maps it to a status.
+int cuda_status(cudaError_t err);
+
+}  // namespace bloth

@@ -1,0 +1,114 @@
+// Launch bookkeeping shared by every entry point (SM count and occupancy
+// caches, CUDA error capture) and the deterministic weight-gradient reduce.
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "common.cuh"
+#include "rows_impl.cuh"
+
+namespace bloth {
+
+static thread_local int g_last_cuda_error = 0;
+
+int cuda_status(cudaError_t err) {
+  if (err == cudaSuccess) return BLOTH_OK;
+  g_last_cuda_error = (int)err;
+  return BLOTH_ERR_CUDA;
+}
+
+int last_cuda_error() { return g_last_cuda_error; }
+
+static int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return -1;
+  }
+  return dev;
+}
+
+int device_sm_count() {
+  static std::mutex mu;
+  static std::map<int, int> cache;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (dev < 0 || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  if (n <= 0) return 1;  // not cached: no usable device yet
+  cache[dev] = n;
+  return n;
+}
+
+int occupancy(const void* func, int block, size_t smem) {
+  using Key = std::tuple<int, const void*, int, size_t>;
+  static std::mutex mu;
+  static std::map<Key, int> cache;
+  const int dev = current_device();
+  const Key key{dev, func, block, smem};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int n = 0;
+  if (dev < 0 ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, block, smem) != cudaSuccess) {
+    cudaGetLastError();
+    return 1;
+  }
+  if (n <= 0) n = 1;
+  std::lock_guard<std::mutex> lk(mu);
+  cache[key] = n;
+  return n;
+}
+
+// Column sums of P accumulator rows of N: CTA x handles 32 columns; warp wi
+// sums rows wi, wi+8, ... in order, then warp 0 adds the 8 warp totals in
+// order, so the result does not depend on scheduling. Columns [0, n0) go to
+// dw0 and [n0, N) to dw1 (skipped when dw1 is NULL), cast to w_dt.
+template <typename AccT>
+__global__ void __launch_bounds__(256)
+    dw_reduce_kernel(const AccT* __restrict__ part, int64_t P, int N, void* dw0, int n0, void* dw1,
+                     int w_dt) {
+  __shared__ double sm[8][32];
+  const int lane = threadIdx.x & 31;
+  const int wi = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  double s = 0.0;
+  if (col < N) {
+#pragma unroll 4
+    for (int64_t p = wi; p < P; p += 8) s += (double)part[p * N + col];
+  }
+  sm[wi][lane] = s;
+  __syncthreads();
+  if (wi == 0 && col < N) {
+    double t = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += sm[i][lane];
+    const float v = (float)t;
+    if (col < n0) st_any(dw0, col, w_dt, v);
+    else if (dw1 != nullptr) st_any(dw1, col - n0, w_dt, v);
+  }
+}
+
+template <typename AccT>
+int launch_dw_reduce(const AccT* part, int64_t P, int N, void* dw0, int n0, void* dw1, int w_dt,
+                     cudaStream_t st) {
+  if (N <= 0) return BLOTH_OK;
+  const unsigned grid = (unsigned)((N + 31) / 32);
+  dw_reduce_kernel<AccT><<<grid, 256, 0, st>>>(part, P, N, dw0, n0, dw1, w_dt);
+  return cuda_status(cudaGetLastError());
+}
+
+template int launch_dw_reduce<float>(const float*, int64_t, int, void*, int, void*, int,
+                                     cudaStream_t);
+template int launch_dw_reduce<double>(const double*, int64_t, int, void*, int, void*, int,
+                                      cudaStream_t);
+
+}  // namespace bloth

@@ -1,0 +1,179 @@
+/*
+ * bloth_b200.h - C ABI of the B200 (sm_100a) RMSNorm and fused RMSNorm+RoPE kernels.
+ *
+ * Plain C: raw device pointers, element strides, an element-type code and a
+ * cudaStream_t passed as void*. Nothing here allocates; the caller owns every
+ * buffer, including the weight-gradient workspace whose size the
+ * *_workspace_bytes() functions report. Every entry point is asynchronous on
+ * the given stream, returns BLOTH_OK or a status code (never aborts), and
+ * keeps no state between calls apart from per-device launch caches. The
+ * device used is the calling thread's current CUDA device.
+ *
+ * Row convention (as in the reference's Triton kernels): a "row" is one
+ * normalised vector of N elements; x[row, col] is at x + row*ldx + col.
+ * Head convention (per-head q/k kernels): element [b, s, h, d] of a
+ * [B, S, H, D] head tensor is at ptr + b*strides[0] + s*strides[1] +
+ * h*strides[2] + d, i.e. the head dimension is contiguous.
+ */
+#ifndef BLOTH_B200_H_
+#define BLOTH_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define BLOTH_F32 0
+#define BLOTH_BF16 1
+#define BLOTH_F16 2
+#define BLOTH_I32 3
+#define BLOTH_I64 4
+
+/* status codes */
+#define BLOTH_OK 0
+#define BLOTH_ERR_DTYPE 1     /* unsupported element-type combination */
+#define BLOTH_ERR_SHAPE 2     /* size out of the supported range, or inconsistent sizes */
+#define BLOTH_ERR_ALIGN 3     /* a pointer or stride the kernel cannot address */
+#define BLOTH_ERR_WORKSPACE 4 /* workspace missing or smaller than *_workspace_bytes() */
+#define BLOTH_ERR_NULL 5      /* a required pointer is NULL */
+#define BLOTH_ERR_CUDA 6      /* the CUDA runtime reported an error; see bloth_last_cuda_error() */
+#define BLOTH_ERR_ARG 7       /* contradictory arguments (e.g. both cos/sin tables and inv_freq) */
+
+/* Largest row length of the row kernels (the reference's limit,
+   bloth/bloth/kernels/rms_norm.py:21 MAX_FUSED_SIZE): 65536 for 16-bit
+   rows, 32768 for fp32 rows. Rows whose base or stride is not 16-byte
+   aligned run on a scalar path limited to 8192. */
+#define BLOTH_MAX_ROW 65536
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int bloth_version(void);
+
+/* Human-readable text of a status code (static storage). */
+const char* bloth_strerror(int status);
+
+/* cudaError_t of the last failing CUDA call made by the calling thread inside
+   this library (0 if none). */
+int bloth_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------
+ * RMSNorm over rows of N: y = x * rsqrt(mean(x^2) + eps) * w, computed in
+ * fp32 and rounded once to the type of x; rstd[M] (fp32) saved for backward.
+ * Replaces the _rms_norm_fwd_kernel launch of _RMSNormFunction.forward
+ * (bloth/bloth/kernels/rms_norm.py:119-140; kernel :39-73).
+ * dtype: type of x and y (F32, BF16, F16); w_dtype: type of w (F32 or dtype).
+ * ---------------------------------------------------------------------- */
+int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy,
+                      float* rstd, int64_t M, int64_t N, float eps, int dtype, int w_dtype,
+                      void* stream);
+
+/* Bytes of workspace bloth_rmsnorm_bwd needs for M rows of N on the current
+   device (per-CTA weight-gradient partial sums). */
+size_t bloth_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N, int dtype);
+
+/* RMSNorm backward: dx = rstd * (dy*w - xhat * mean(dy*w*xhat)), xhat = x*rstd,
+   and dw = sum over rows of dy*xhat written in w_dtype. dw is reduced
+   deterministically (per-CTA partials in the workspace, then a fixed-order
+   sum), not with atomics.
+   Replaces _RMSNormFunction.backward (bloth/bloth/kernels/rms_norm.py:143-160;
+   kernel :76-113). */
+int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
+                      const float* rstd, void* dx, int64_t lddx, void* dw, int64_t M, int64_t N,
+                      int dtype, int w_dtype, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused RMSNorm + rotate-half RoPE with per-row cos/sin tables, the
+ * reference's fused_norm_rope(x, weight, cos, sin, eps) contract: each row of
+ * N is RMS-normalised over all N columns; columns [0, 2*half) are rotated in
+ * pairs (c, c+half) with cos/sin[row, c]: y1 = n1*cos - n2*sin,
+ * y2 = n1*sin + n2*cos; columns >= 2*half are only normalised.
+ * cos/sin: [M, half] with row stride ldcs, type cs_dtype (F32, BF16, F16).
+ * Replaces _FusedNormRoPEFunction.forward
+ * (bloth/bloth/kernels/fused_norm_qkv_rope.py:132-159; kernel :40-96).
+ * ---------------------------------------------------------------------- */
+int bloth_norm_rope_fwd(const void* x, int64_t ldx, const void* w, const void* cos,
+                        const void* sin, int64_t ldcs, int cs_dtype, int64_t half, void* y,
+                        int64_t ldy, float* rstd, int64_t M, int64_t N, float eps, int dtype,
+                        int w_dtype, void* stream);
+
+size_t bloth_norm_rope_bwd_workspace_bytes(int64_t M, int64_t N, int dtype);
+
+/* Backward of bloth_norm_rope_fwd: applies the transposed rotation to dy,
+   then the RMSNorm backward; dw in w_dtype. This is the gradient of the
+   forward above; the reference's _fused_norm_rope_bwd_kernel
+   (bloth/bloth/kernels/fused_norm_qkv_rope.py:99-126) omits the rotation.
+   Replaces _FusedNormRoPEFunction.backward (:161-176). */
+int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
+                        const void* cos, const void* sin, int64_t ldcs, int cs_dtype,
+                        int64_t half, const float* rstd, void* dx, int64_t lddx, void* dw,
+                        int64_t M, int64_t N, int dtype, int w_dtype, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Per-head q/k RMSNorm + RoPE over [B, S, H, D] head tensors in one launch.
+ * Each (token, head) row of D is normalised with its tensor's weight (wq for
+ * q, wk for k), then rotated in pairs (d, d + D/2) by the angle of the
+ * token's position. cos/sin come from exactly one of:
+ *   - inv_freq [D/2] fp32: angle = float(pos) * inv_freq[i] rounded to fp32,
+ *     cos/sin evaluated in-register once per token and shared by all heads;
+ *   - cos/sin tables: row = table + b*cs_strides[0] + p*cs_strides[1], with
+ *     p = pos[b, s] (or s when pos is NULL); elements [0, D/2) of the row are
+ *     used, so full-width [.., D] tables with duplicated halves also work.
+ * pos: [B, S] positions (I64 or I32) at pos + b*pos_strides[0] +
+ *   s*pos_strides[1]; NULL means pos = s. Packed sequences pass positions that
+ *   restart at each document.
+ * rstd_q [B*S*Hq], rstd_k [B*S*Hk]: fp32, token-major, saved for backward.
+ * k, wk, k_out, rstd_k may be NULL when Hk == 0. D: 64, 128 or 256.
+ * New entry point with no single counterpart in the reference: it fuses the
+ * reference's per-row fused_norm_rope (fused_norm_qkv_rope.py:40-96) for both
+ * tensors with the cos/sin construction of BlothRoPE._build_cache
+ * (bloth/bloth/ops/rope.py:71-77), replacing the HF q_norm/k_norm +
+ * apply_rotary_pos_emb pair that patch_model leaves in place (patch.py:46-76).
+ * ---------------------------------------------------------------------- */
+int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* k,
+                           const int64_t* k_strides, const void* wq, const void* wk, void* q_out,
+                           const int64_t* qo_strides, void* k_out, const int64_t* ko_strides,
+                           float* rstd_q, float* rstd_k, const void* pos,
+                           const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
+                           const void* cos, const void* sin, const int64_t* cs_strides,
+                           int cs_dtype, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
+                           float eps, int dtype, int w_dtype, void* stream);
+
+size_t bloth_qk_norm_rope_bwd_workspace_bytes(int64_t B, int64_t S, int64_t D, int dtype);
+
+/* Backward of bloth_qk_norm_rope_fwd: dq, dk (same layout rules) and the
+   weight gradients dwq, dwk [D] in w_dtype (reduced deterministically through
+   the workspace). dk, dwk may be NULL when Hk == 0. */
+int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const void* dk_out,
+                           const int64_t* dko_strides, const void* q, const int64_t* q_strides,
+                           const void* k, const int64_t* k_strides, const void* wq,
+                           const void* wk, const float* rstd_q, const float* rstd_k, void* dq,
+                           const int64_t* dq_strides, void* dk, const int64_t* dk_strides,
+                           void* dwq, void* dwk, const void* pos, const int64_t* pos_strides,
+                           int pos_dtype, const float* inv_freq, const void* cos,
+                           const void* sin, const int64_t* cs_strides, int cs_dtype, int64_t B,
+                           int64_t S, int64_t Hq, int64_t Hk, int64_t D, int dtype, int w_dtype,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Rotate-half RoPE alone over a [B, S, H, D] head tensor (same cos/sin and
+ * position rules as above). transpose = 0 applies the rotation
+ * (y1 = x1*cos - x2*sin, y2 = x1*sin + x2*cos); transpose = 1 applies its
+ * transpose, which is the backward (dx from dy).
+ * Replaces rope_embedding / _rope_kernel (bloth/bloth/ops/rope.py:9-58), which
+ * is forward-only and always stores bf16; here the output has x's type.
+ * ---------------------------------------------------------------------- */
+int bloth_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_strides,
+               const void* pos, const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
+               const void* cos, const void* sin, const int64_t* cs_strides, int cs_dtype,
+               int64_t B, int64_t S, int64_t H, int64_t D, int transpose, int dtype,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BLOTH_B200_H_ */

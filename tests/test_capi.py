@@ -1,0 +1,133 @@
+"""The C-ABI library loads without a GPU and exports every declared entry
+point; host-side argument handling raises the reference's errors. CPU only:
+no kernel is launched here."""
+import os
+import re
+
+import pytest
+import torch
+
+import bloth_b200
+from bloth_b200 import _lib
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                      "bloth_b200.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(bloth_\w+)\s*\(", text)))
+
+
+def test_library_built_and_loads():
+    assert os.path.exists(_lib.LIB_PATH), "run python -m bloth_b200.build"
+    lib = _lib.load()
+    assert lib.bloth_version() == (0 << 16) | (1 << 8) | 0
+
+
+def test_every_declared_symbol_is_exported_and_bound():
+    syms = declared_symbols()
+    assert len(syms) >= 12
+    lib = _lib.load()
+    for s in syms:
+        assert hasattr(lib, s), s
+    assert sorted(_lib.exported_symbols()) == syms
+
+
+def test_strerror_texts():
+    lib = _lib.load()
+    for code in range(0, 8):
+        assert lib.bloth_strerror(code)
+    assert lib.bloth_strerror(999) == b"unknown status"
+
+
+def test_validation_errors_without_gpu():
+    # argument checks run before any CUDA call, so they answer on a CPU host
+    lib = _lib.load()
+    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 1, 70000, 1e-6, 1, 1, None) == 2
+    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 1, 40000, 1e-6, 0, 0, None) == 2
+    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 1, 64, 1e-6, 7, 1, None) == 1
+    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 4, 64, 1e-6, 1, 1, None) == 5
+    # M == 0 is a no-op
+    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 0, 64, 1e-6, 1, 1, None) == 0
+    # rotated part wider than the row
+    assert lib.bloth_norm_rope_fwd(None, 0, None, None, None, 0, 0, 40, None, 0, None, 4, 64,
+                                   1e-6, 1, 1, None) == 2
+    # head_dim outside {64, 128, 256}
+    st = _lib.strides((0, 0, 0))
+    assert lib.bloth_rope(None, st, None, st, None, None, 0, None, None, None, None, 0, 1, 1, 1,
+                          96, 0, 1, None) == 2
+    # both a table and inv_freq
+    dummy = _lib.ptr(torch.zeros(1))
+    assert lib.bloth_rope(None, st, None, st, None, None, 0, dummy, dummy, dummy, st, 0, 1, 1, 1,
+                          64, 0, 1, None) == 7
+
+
+def test_cpu_tensors_raise_like_the_reference():
+    x = torch.randn(4, 64)
+    w = torch.ones(64)
+    with pytest.raises(AssertionError, match="CUDA GPU required"):
+        bloth_b200.kernels.fused_norm_rope(x, w, torch.ones(4, 32), torch.zeros(4, 32))
+    with pytest.raises(AssertionError, match="CUDA GPU required"):
+        bloth_b200.rms_norm(x, w)
+    with pytest.raises(AssertionError, match="CUDA GPU required"):
+        bloth_b200.fused_qk_norm_rope(torch.randn(1, 2, 2, 64), None, w, None)
+
+
+def test_row_limit_error_like_the_reference():
+    from bloth_b200.kernels.rms_norm import _check_row
+    with pytest.raises(RuntimeError, match="exceeds max"):
+        _check_row(65537, torch.bfloat16)
+    with pytest.raises(RuntimeError, match="exceeds max"):
+        _check_row(32769, torch.float32)
+    _check_row(65536, torch.bfloat16)
+
+
+def test_reference_name_surface():
+    for name in ("rms_norm", "BlothRMSNorm", "fused_norm_qkv", "BlothFusedNormQKV",
+                 "rope_embedding", "BlothRoPE", "patch_model", "FastModel"):
+        assert hasattr(bloth_b200, name), name
+    k = bloth_b200.kernels
+    assert k.bloth_rms_norm is k.rms_norm
+    for name in ("rms_norm", "bloth_rms_norm", "fused_norm_rope", "rope_embedding"):
+        assert hasattr(k, name), name
+
+
+def test_position_and_table_parsing():
+    from bloth_b200.kernels.fused_norm_qkv_rope import _positions, _tables
+    p, st = _positions(torch.arange(16), 3, 16)
+    assert list(st) == [0, 1] and p.dtype == torch.int64
+    p, st = _positions(torch.arange(32, dtype=torch.int32).view(2, 16), 2, 16)
+    assert list(st) == [16, 1] and p.dtype == torch.int32
+    with pytest.raises(ValueError):
+        _positions(torch.arange(15), 1, 16)
+    c = torch.randn(100, 64)
+    _, _, st, tok = _tables(c, c.clone(), 2, 16, 128)
+    assert list(st) == [0, 64] and not tok
+    c = torch.randn(2, 16, 128)
+    _, _, st, tok = _tables(c, c.clone(), 2, 16, 128)
+    assert list(st) == [16 * 128, 128] and tok
+    c = torch.randn(1, 16, 128)
+    _, _, st, tok = _tables(c, c.clone(), 4, 16, 128)
+    assert list(st) == [0, 128] and tok
+    with pytest.raises(ValueError):
+        _tables(torch.randn(16, 48), torch.randn(16, 48), 1, 16, 128)
+
+
+def test_patch_model_swaps_norms_and_shares_weights():
+    transformers = pytest.importorskip("transformers")
+    cfg = transformers.Qwen3Config(vocab_size=64, hidden_size=64, intermediate_size=128,
+                                   num_hidden_layers=2, num_attention_heads=4,
+                                   num_key_value_heads=2, head_dim=16)
+    model = transformers.Qwen3ForCausalLM(cfg)
+    before = {n: m.weight for n, m in model.named_modules()
+              if type(m).__name__ == "Qwen3RMSNorm"}
+    keys = set(model.state_dict())
+    bloth_b200.patch_model(model, verbose=False)
+    after = {n: m for n, m in model.named_modules() if type(m).__name__ == "BlothRMSNorm"}
+    # 2 layers x (input, post-attention, q_norm, k_norm) + final norm
+    assert len(before) == len(after) == 9
+    for n, m in after.items():
+        assert m.weight is before[n]
+    assert set(model.state_dict()) == keys
