@@ -52,15 +52,15 @@ _SIGNATURES = {
     "bloth_norm_rope_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _int, _i64, _vp, _vp,
                                    _i64, _vp, _i64, _i64, _int, _int, _vp, _sz, _vp]),
     "bloth_qk_norm_rope_fwd": (_int, [_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
-                                      _vp, _vp, _vp, _i64p, _int, _vp, _vp, _vp, _i64p, _int,
-                                      _i64, _i64, _i64, _i64, _i64, _f32, _int, _int, _vp]),
+                                      _vp, _vp, _vp, _i64p, _int, _vp, _vp, _vp, _i64p, _i64,
+                                      _int, _i64, _i64, _i64, _i64, _i64, _f32, _int, _int, _vp]),
     "bloth_qk_norm_rope_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _int]),
     "bloth_qk_norm_rope_bwd": (_int, [_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
                                       _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p,
-                                      _int, _vp, _vp, _vp, _i64p, _int, _i64, _i64, _i64, _i64,
-                                      _i64, _int, _int, _vp, _sz, _vp]),
-    "bloth_rope": (_int, [_vp, _i64p, _vp, _i64p, _vp, _i64p, _int, _vp, _vp, _vp, _i64p, _int,
-                          _i64, _i64, _i64, _i64, _int, _int, _vp]),
+                                      _int, _vp, _vp, _vp, _i64p, _i64, _int, _i64, _i64, _i64,
+                                      _i64, _i64, _int, _int, _vp, _sz, _vp]),
+    "bloth_rope": (_int, [_vp, _i64p, _vp, _i64p, _vp, _i64p, _int, _vp, _vp, _vp, _i64p, _i64,
+                          _int, _i64, _i64, _i64, _i64, _int, _int, _vp]),
 }
 
 

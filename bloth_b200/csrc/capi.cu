@@ -106,7 +106,8 @@ HT make_ht(const void* p, const int64_t* st) {
 // Position and cos/sin source shared by the per-head entry points.
 int fill_rope_source(HeadArgs& a, const void* pos, const int64_t* pos_strides, int pos_dtype,
                      const float* inv_freq, const void* cos, const void* sin,
-                     const int64_t* cs_strides, int cs_dtype, int dtype, int64_t D) {
+                     const int64_t* cs_strides, int64_t cs_rows, int cs_dtype, int dtype,
+                     int64_t D) {
   a.pos = pos;
   if (pos != nullptr) {
     if (pos_dtype != BLOTH_I64 && pos_dtype != BLOTH_I32) return BLOTH_ERR_DTYPE;
@@ -121,6 +122,8 @@ int fill_rope_source(HeadArgs& a, const void* pos, const int64_t* pos_strides, i
   if (table) {
     if (cos == nullptr || sin == nullptr || cs_strides == nullptr) return BLOTH_ERR_NULL;
     if (!is_float_dt(cs_dtype)) return BLOTH_ERR_DTYPE;
+    if (cs_rows < 1) return BLOTH_ERR_SHAPE;
+    a.cs_rows = cs_rows;
     a.cos = cos;
     a.sin = sin;
     a.cs_dt = cs_dtype;
@@ -294,8 +297,8 @@ int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* 
                            float* rstd_q, float* rstd_k, const void* pos,
                            const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
                            const void* cos, const void* sin, const int64_t* cs_strides,
-                           int cs_dtype, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
-                           float eps, int dtype, int w_dtype, void* stream) {
+                           int64_t cs_rows, int cs_dtype, int64_t B, int64_t S, int64_t Hq,
+                           int64_t Hk, int64_t D, float eps, int dtype, int w_dtype, void* stream) {
   if (!is_float_dt(dtype) || !is_float_dt(w_dtype)) return BLOTH_ERR_DTYPE;
   if (!head_dim_ok(D) || B < 0 || S < 0 || Hq < 0 || Hk < 0 || Hq + Hk < 1 || Hq > (1 << 20) ||
       Hk > (1 << 20))
@@ -303,7 +306,7 @@ int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* 
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
-                            cs_dtype, dtype, D);
+                            cs_rows, cs_dtype, dtype, D);
   if (rc) return rc;
   if (B * S == 0) return BLOTH_OK;
   const void* src[2] = {q, k};
@@ -351,9 +354,10 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
                            const int64_t* dq_strides, void* dk, const int64_t* dk_strides,
                            void* dwq, void* dwk, const void* pos, const int64_t* pos_strides,
                            int pos_dtype, const float* inv_freq, const void* cos,
-                           const void* sin, const int64_t* cs_strides, int cs_dtype, int64_t B,
-                           int64_t S, int64_t Hq, int64_t Hk, int64_t D, int dtype, int w_dtype,
-                           void* workspace, size_t workspace_bytes, void* stream) {
+                           const void* sin, const int64_t* cs_strides, int64_t cs_rows,
+                           int cs_dtype, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
+                           int dtype, int w_dtype, void* workspace, size_t workspace_bytes,
+                           void* stream) {
   if (!is_float_dt(dtype) || !is_float_dt(w_dtype)) return BLOTH_ERR_DTYPE;
   if (!head_dim_ok(D) || B < 0 || S < 0 || Hq < 0 || Hk < 0 || Hq + Hk < 1 || Hq > (1 << 20) ||
       Hk > (1 << 20))
@@ -361,7 +365,7 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
-                            cs_dtype, dtype, D);
+                            cs_rows, cs_dtype, dtype, D);
   if (rc) return rc;
   const void* g[2] = {dq_out, dk_out};
   const int64_t* gst[2] = {dqo_strides, dko_strides};
@@ -400,15 +404,15 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
 
 int bloth_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_strides,
                const void* pos, const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
-               const void* cos, const void* sin, const int64_t* cs_strides, int cs_dtype,
-               int64_t B, int64_t S, int64_t H, int64_t D, int transpose, int dtype,
+               const void* cos, const void* sin, const int64_t* cs_strides, int64_t cs_rows,
+               int cs_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int transpose, int dtype,
                void* stream) {
   if (!is_float_dt(dtype)) return BLOTH_ERR_DTYPE;
   if (!head_dim_ok(D) || B < 0 || S < 0 || H < 1 || H > (1 << 20)) return BLOTH_ERR_SHAPE;
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
-                            cs_dtype, dtype, D);
+                            cs_rows, cs_dtype, dtype, D);
   if (rc) return rc;
   if (B * S == 0) return BLOTH_OK;
   if ((rc = check_heads_tensor(x, x_strides, dtype))) return rc;

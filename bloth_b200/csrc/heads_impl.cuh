@@ -53,6 +53,7 @@ struct HeadArgs {
   int cs_dt;
   int cs_vec;
   int64_t cs_sb, cs_sp;
+  int64_t cs_rows;  // rows of a table indexed by position; p is clamped to [0, cs_rows)
   int64_t B, S;
   float eps;
   int transpose;  // RoPE-only: apply R^T
@@ -124,7 +125,8 @@ __device__ __forceinline__ void token_cos_sin(const HeadArgs& a, int64_t b, int6
                                               float (&sn)[HG<T, D>::VEC]) {
   using G = HG<T, D>;
   if (a.cos != nullptr) {
-    const int64_t off = b * a.cs_sb + p * a.cs_sp + (int64_t)pg * G::VEC;
+    const int64_t pr = p < 0 ? 0 : (p >= a.cs_rows ? a.cs_rows - 1 : p);
+    const int64_t off = b * a.cs_sb + pr * a.cs_sp + (int64_t)pg * G::VEC;
     ld_any_vec<G::VEC>(a.cos, off, a.cs_dt, a.cs_vec != 0, cs);
     ld_any_vec<G::VEC>(a.sin, off, a.cs_dt, a.cs_vec != 0, sn);
   } else {

@@ -131,25 +131,25 @@ def _positions(position_ids, B: int, S: int):
 
 
 def _tables(cos, sin, B: int, S: int, D: int):
-    """(cos, sin, strides[2], token_indexed) for cos/sin tables.
+    """(cos, sin, strides[2], rows, token_indexed) for cos/sin tables.
 
     [P, D/2] or [P, D] tables are indexed by position; [B|1, S, D/2|D] tables
     (HuggingFace's position_embeddings) are indexed by token."""
     if cos is None and sin is None:
-        return None, None, None, False
+        return None, None, None, 0, False
     if cos is None or sin is None or cos.shape != sin.shape:
         raise ValueError("[Bloth] cos and sin must be given together with equal shapes")
     if cos.shape[-1] not in (D // 2, D):
         raise ValueError(f"[Bloth] cos/sin last dim must be {D // 2} or {D}")
     cos = _lib.aligned16(cos if cos.stride(-1) == 1 else cos.contiguous())
     sin = _lib.aligned16(sin if sin.stride(-1) == 1 else sin.contiguous())
+    if cos.stride() != sin.stride():
+        cos, sin = _lib.aligned16(cos.contiguous()), _lib.aligned16(sin.contiguous())
     if cos.dim() == 2:
-        return cos, sin, _lib.strides((0, cos.stride(0))), False
+        return cos, sin, _lib.strides((0, cos.stride(0))), cos.shape[0], False
     if cos.dim() == 3 and cos.shape[1] == S and cos.shape[0] in (1, B):
-        if cos.stride() != sin.stride():
-            cos, sin = cos.contiguous(), sin.contiguous()
         sb = 0 if cos.shape[0] == 1 else cos.stride(0)
-        return cos, sin, _lib.strides((sb, cos.stride(1))), True
+        return cos, sin, _lib.strides((sb, cos.stride(1))), S, True
     raise ValueError(f"[Bloth] unsupported cos/sin shape {tuple(cos.shape)}")
 
 
@@ -167,7 +167,7 @@ class _QKNormRoPEFunction(torch.autograd.Function):
         if k4 is not None and (k4.shape[0] != B or k4.shape[1] != S or k4.shape[3] != D):
             raise ValueError("[Bloth] q and k must share batch, sequence and head_dim")
         pos, pos_st = _positions(position_ids, B, S)
-        cos, sin, cs_st, token_idx = _tables(cos, sin, B, S, D)
+        cos, sin, cs_st, cs_rows, token_idx = _tables(cos, sin, B, S, D)
         if (cos is None) == (inv_freq is None):
             raise ValueError("[Bloth] give exactly one of inv_freq or cos/sin")
         if inv_freq is not None:
@@ -189,13 +189,13 @@ class _QKNormRoPEFunction(torch.autograd.Function):
             _lib.ptr(ko), _head_strides(ko), _lib.ptr(rq), _lib.ptr(rk), _lib.ptr(kpos),
             pos_st if kpos is not None else None,
             _lib.dtype_code(kpos.dtype) if kpos is not None else 0, _lib.ptr(inv_freq),
-            _lib.ptr(cos), _lib.ptr(sin), cs_st, _lib.dtype_code(cos.dtype) if cos is not None else 0,
-            B, S, Hq, Hk, D, float(eps), _lib.dtype_code(q4.dtype), _lib.dtype_code(wq.dtype),
+            _lib.ptr(cos), _lib.ptr(sin), cs_st, cs_rows,
+            _lib.dtype_code(cos.dtype) if cos is not None else 0, B, S, Hq, Hk, D, float(eps), _lib.dtype_code(q4.dtype), _lib.dtype_code(wq.dtype),
             _lib.stream_of(q4))
         _lib.check(rc, "qk norm+rope forward")
         ctx.save_for_backward(q4, k4, wq, wk, rq, rk, kpos, inv_freq, cos, sin)
-        ctx.meta = (B, S, Hq, Hk, D, pos_st if kpos is not None else None, cs_st, shape_q,
-                    shape_k)
+        ctx.meta = (B, S, Hq, Hk, D, pos_st if kpos is not None else None, cs_st, cs_rows,
+                    shape_q, shape_k)
         if k4 is None:
             return qo.view(shape_q)
         return qo.view(shape_q), ko.view(shape_k)
@@ -203,7 +203,7 @@ class _QKNormRoPEFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, *grads):
         q4, k4, wq, wk, rq, rk, pos, inv_freq, cos, sin = ctx.saved_tensors
-        B, S, Hq, Hk, D, pos_st, cs_st, shape_q, shape_k = ctx.meta
+        B, S, Hq, Hk, D, pos_st, cs_st, cs_rows, shape_q, shape_k = ctx.meta
         gq = _heads(grads[0].reshape(q4.shape) if grads[0].dim() != 4 else grads[0])
         gk = None
         if k4 is not None:
@@ -224,7 +224,7 @@ class _QKNormRoPEFunction(torch.autograd.Function):
             _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(rq), _lib.ptr(rk), _lib.ptr(dq),
             _head_strides(dq), _lib.ptr(dk), _head_strides(dk), _lib.ptr(dwq), _lib.ptr(dwk),
             _lib.ptr(pos), pos_st, _lib.dtype_code(pos.dtype) if pos is not None else 0,
-            _lib.ptr(inv_freq), _lib.ptr(cos), _lib.ptr(sin), cs_st,
+            _lib.ptr(inv_freq), _lib.ptr(cos), _lib.ptr(sin), cs_st, cs_rows,
             _lib.dtype_code(cos.dtype) if cos is not None else 0, B, S, Hq, Hk, D,
             _lib.dtype_code(q4.dtype), _lib.dtype_code(wq.dtype), _lib.ptr(ws), ws_bytes,
             _lib.stream_of(q4))

@@ -120,8 +120,9 @@ int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx
  *   - inv_freq [D/2] fp32: angle = float(pos) * inv_freq[i] rounded to fp32,
  *     cos/sin evaluated in-register once per token and shared by all heads;
  *   - cos/sin tables: row = table + b*cs_strides[0] + p*cs_strides[1], with
- *     p = pos[b, s] (or s when pos is NULL); elements [0, D/2) of the row are
- *     used, so full-width [.., D] tables with duplicated halves also work.
+ *     p = pos[b, s] (or s when pos is NULL) clamped to [0, cs_rows - 1];
+ *     elements [0, D/2) of the row are used, so full-width [.., D] tables
+ *     with duplicated halves also work.
  * pos: [B, S] positions (I64 or I32) at pos + b*pos_strides[0] +
  *   s*pos_strides[1]; NULL means pos = s. Packed sequences pass positions that
  *   restart at each document.
@@ -139,8 +140,8 @@ int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* 
                            float* rstd_q, float* rstd_k, const void* pos,
                            const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
                            const void* cos, const void* sin, const int64_t* cs_strides,
-                           int cs_dtype, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
-                           float eps, int dtype, int w_dtype, void* stream);
+                           int64_t cs_rows, int cs_dtype, int64_t B, int64_t S, int64_t Hq,
+                           int64_t Hk, int64_t D, float eps, int dtype, int w_dtype, void* stream);
 
 size_t bloth_qk_norm_rope_bwd_workspace_bytes(int64_t B, int64_t S, int64_t D, int dtype);
 
@@ -154,9 +155,10 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
                            const int64_t* dq_strides, void* dk, const int64_t* dk_strides,
                            void* dwq, void* dwk, const void* pos, const int64_t* pos_strides,
                            int pos_dtype, const float* inv_freq, const void* cos,
-                           const void* sin, const int64_t* cs_strides, int cs_dtype, int64_t B,
-                           int64_t S, int64_t Hq, int64_t Hk, int64_t D, int dtype, int w_dtype,
-                           void* workspace, size_t workspace_bytes, void* stream);
+                           const void* sin, const int64_t* cs_strides, int64_t cs_rows,
+                           int cs_dtype, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
+                           int dtype, int w_dtype, void* workspace, size_t workspace_bytes,
+                           void* stream);
 
 /* ------------------------------------------------------------------------
  * Rotate-half RoPE alone over a [B, S, H, D] head tensor (same cos/sin and
@@ -168,8 +170,8 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
  * ---------------------------------------------------------------------- */
 int bloth_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_strides,
                const void* pos, const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
-               const void* cos, const void* sin, const int64_t* cs_strides, int cs_dtype,
-               int64_t B, int64_t S, int64_t H, int64_t D, int transpose, int dtype,
+               const void* cos, const void* sin, const int64_t* cs_strides, int64_t cs_rows,
+               int cs_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int transpose, int dtype,
                void* stream);
 
 #ifdef __cplusplus

@@ -148,9 +148,9 @@ def _head_cos_sin(pos, inv_f, cos_tab, sin_tab, compute, D):
     return c.unsqueeze(-2), s.unsqueeze(-2)
 
 
-def _positions(B: int, S: int, position_ids):
+def _positions(B: int, S: int, position_ids, device=None):
     if position_ids is None:
-        return torch.arange(S, dtype=torch.int64).expand(B, S)
+        return torch.arange(S, dtype=torch.int64, device=device).expand(B, S)
     p = position_ids.to(torch.int64)
     if p.dim() == 1:
         p = p.unsqueeze(0)
@@ -167,7 +167,7 @@ def qk_norm_rope(q, k, wq, wk, position_ids=None, inv_f=None, eps: float = 1e-6,
     rstd_k); rstd are float32 [B, S, H].
     """
     B, S, _, D = q.shape
-    pos = _positions(B, S, position_ids)
+    pos = _positions(B, S, position_ids, q.device)
     c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
     outs = []
     for x, w in ((q, wq), (k, wk)):
@@ -186,7 +186,7 @@ def qk_norm_rope_fwd_bwd(q, k, wq, wk, dq_out, dk_out, position_ids=None, inv_f=
     Returns dict with q_out, k_out, rstd_q, rstd_k, dq, dk, dwq, dwk.
     """
     B, S, _, D = q.shape
-    pos = _positions(B, S, position_ids)
+    pos = _positions(B, S, position_ids, q.device)
     c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
     res = {}
     for name, x, w, g in (("q", q, wq, dq_out), ("k", k, wk, dk_out)):
@@ -209,7 +209,7 @@ def rope(x, position_ids=None, inv_f=None, cos=None, sin=None, compute=F64,
          out_dtype=None):
     """Rotate-half RoPE of x [B, S, H, D] - bloth/bloth/ops/rope.py:21-27."""
     B, S, _, D = x.shape
-    pos = _positions(B, S, position_ids)
+    pos = _positions(B, S, position_ids, x.device)
     c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
     y = _rotate(x.to(compute), c, s, D // 2)
     return y.to(out_dtype or x.dtype)
@@ -218,7 +218,7 @@ def rope(x, position_ids=None, inv_f=None, cos=None, sin=None, compute=F64,
 def rope_fwd_bwd(x, dy, position_ids=None, inv_f=None, cos=None, sin=None, compute=F64):
     """RoPE forward and its exact backward (the transposed rotation)."""
     B, S, _, D = x.shape
-    pos = _positions(B, S, position_ids)
+    pos = _positions(B, S, position_ids, x.device)
     c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
     xc = x.detach().to(compute).requires_grad_(True)
     y = _rotate(xc, c, s, D // 2)
@@ -250,19 +250,55 @@ def packed_position_ids(rows: int, tokens: int, lo: int, hi: int, generator) -> 
     return out
 
 
+def rms_norm_dw_scale(x, dy, eps: float = 1e-6, compute=F64):
+    """Per-column root-sum-square of the weight-gradient terms dy * xhat.
+
+    The error of any fp32 evaluation of dweight = sum_rows(dy * xhat) grows
+    with this quantity (each term carries a relative rounding error), not
+    with |dweight|, which can be far smaller after cancellation.
+    """
+    xc = x.to(compute)
+    rstd = 1.0 / torch.sqrt((xc * xc).mean(-1, keepdim=True) + eps)
+    t = dy.to(compute) * xc * rstd
+    return torch.sqrt((t * t).reshape(-1, x.shape[-1]).sum(0))
+
+
+def qk_dw_scale(x, dy, position_ids=None, inv_f=None, eps: float = 1e-6, cos=None, sin=None,
+                compute=F64):
+    """Per-column root-sum-square of the terms (R^T dy) * xhat of a head
+    tensor's weight gradient (see :func:`rms_norm_dw_scale`)."""
+    B, S, _, D = x.shape
+    pos = _positions(B, S, position_ids, x.device)
+    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
+    g = dy.to(compute)
+    h = D // 2
+    g1, g2 = g[..., :h], g[..., h:]
+    dn = torch.cat([g1 * c + g2 * s, g2 * c - g1 * s], -1)
+    xc = x.to(compute)
+    rstd = 1.0 / torch.sqrt((xc * xc).mean(-1, keepdim=True) + eps)
+    t = dn * xc * rstd
+    return torch.sqrt((t * t).reshape(-1, D).sum(0))
+
+
 def tolerance_ok(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype,
-                 scale_with_magnitude: bool = False) -> tuple[bool, float]:
+                 scale_with_magnitude: bool = False, scale: torch.Tensor | None = None
+                 ) -> tuple[bool, float]:
     """Elementwise tolerance of the path: fp32 max abs <= 1e-5; bf16/fp16 abs
     <= 2e-2 or rel <= 1.6e-2. With ``scale_with_magnitude`` the fp32 bound
     becomes 1e-5 * max(1, |ref|) (values whose magnitude puts 1e-5 below
     fp32 resolution, e.g. weight gradients summed over millions of rows, or
-    rows of zeros where rstd = 1/sqrt(eps)). Returns (ok, worst excess).
+    rows of zeros where rstd = 1/sqrt(eps)); ``scale`` (a per-element
+    magnitude, e.g. :func:`rms_norm_dw_scale` for a weight gradient) raises
+    the fp32 bound to at least 1e-5 * scale. Returns (ok, worst excess).
     """
     g = got.to(F64)
     r = ref.to(F64)
     err = (g - r).abs()
     if dtype == torch.float32:
         bound = 1e-5 * (torch.clamp(r.abs(), min=1.0) if scale_with_magnitude else 1.0)
+        if scale is not None:
+            bound = torch.maximum(torch.as_tensor(bound, dtype=F64, device=r.device),
+                                  1e-5 * scale.to(F64).to(r.device))
         excess = (err - bound)
     else:
         rel = err / r.abs().clamp(min=1e-30)

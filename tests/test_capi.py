@@ -56,12 +56,12 @@ def test_validation_errors_without_gpu():
                                    1e-6, 1, 1, None) == 2
     # head_dim outside {64, 128, 256}
     st = _lib.strides((0, 0, 0))
-    assert lib.bloth_rope(None, st, None, st, None, None, 0, None, None, None, None, 0, 1, 1, 1,
-                          96, 0, 1, None) == 2
+    assert lib.bloth_rope(None, st, None, st, None, None, 0, None, None, None, None, 0, 0, 1, 1,
+                          1, 96, 0, 1, None) == 2
     # both a table and inv_freq
     dummy = _lib.ptr(torch.zeros(1))
-    assert lib.bloth_rope(None, st, None, st, None, None, 0, dummy, dummy, dummy, st, 0, 1, 1, 1,
-                          64, 0, 1, None) == 7
+    assert lib.bloth_rope(None, st, None, st, None, None, 0, dummy, dummy, dummy, st, 1, 0, 1, 1,
+                          1, 64, 0, 1, None) == 7
 
 
 def test_cpu_tensors_raise_like_the_reference():
@@ -103,13 +103,13 @@ def test_position_and_table_parsing():
     with pytest.raises(ValueError):
         _positions(torch.arange(15), 1, 16)
     c = torch.randn(100, 64)
-    _, _, st, tok = _tables(c, c.clone(), 2, 16, 128)
-    assert list(st) == [0, 64] and not tok
+    _, _, st, rows, tok = _tables(c, c.clone(), 2, 16, 128)
+    assert list(st) == [0, 64] and rows == 100 and not tok
     c = torch.randn(2, 16, 128)
-    _, _, st, tok = _tables(c, c.clone(), 2, 16, 128)
-    assert list(st) == [16 * 128, 128] and tok
+    _, _, st, rows, tok = _tables(c, c.clone(), 2, 16, 128)
+    assert list(st) == [16 * 128, 128] and rows == 16 and tok
     c = torch.randn(1, 16, 128)
-    _, _, st, tok = _tables(c, c.clone(), 4, 16, 128)
+    _, _, st, rows, tok = _tables(c, c.clone(), 4, 16, 128)
     assert list(st) == [0, 128] and tok
     with pytest.raises(ValueError):
         _tables(torch.randn(16, 48), torch.randn(16, 48), 1, 16, 128)
