@@ -9,6 +9,7 @@
 
 namespace bloth {
 int last_cuda_error();
+int device_fault(int reset);
 }
 
 using namespace bloth;
@@ -160,6 +161,8 @@ const char* bloth_strerror(int status) {
 
 int bloth_last_cuda_error(void) { return bloth::last_cuda_error(); }
 
+int bloth_device_fault(int reset) { return bloth::device_fault(reset); }
+
 // ---------------------------------------------------------------- RMSNorm
 int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy,
                       float* rstd, int64_t M, int64_t N, float eps, int dtype, int w_dtype,
@@ -305,6 +308,7 @@ int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* 
     return BLOTH_ERR_SHAPE;
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
+  a.fault = fault_word();
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
                             cs_rows, cs_dtype, dtype, D);
   if (rc) return rc;
@@ -364,6 +368,7 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
     return BLOTH_ERR_SHAPE;
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
+  a.fault = fault_word();
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
                             cs_rows, cs_dtype, dtype, D);
   if (rc) return rc;
@@ -396,6 +401,8 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
   a.w_dt = w_dtype;
   a.B = B;
   a.S = S;
+  a.rstd_bulk = (Hq % 4 == 0) && (Hk % 4 == 0) && aligned(rstd_q, 16) &&
+                (Hk == 0 || aligned(rstd_k, 16));
   return dispatch_dtype(dtype, [&](auto t) {
     return heads_bwd<decltype(t)>(a, (int)D, workspace, workspace_bytes, dwq,
                                   Hk > 0 ? dwk : nullptr, as_stream(stream));
@@ -411,6 +418,7 @@ int bloth_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* 
   if (!head_dim_ok(D) || B < 0 || S < 0 || H < 1 || H > (1 << 20)) return BLOTH_ERR_SHAPE;
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
+  a.fault = fault_word();
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
                             cs_rows, cs_dtype, dtype, D);
   if (rc) return rc;

@@ -12,6 +12,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "../../include/bloth_b200.h"
 
 namespace bloth {
@@ -77,11 +79,28 @@ __device__ __forceinline__ void unpack(const Pack<T, VEC>& pk, float (&f)[VEC]) 
   for (int e = 0; e < VEC; ++e) f[e] = to_f(pk.v[e]);
 }
 
+// Rounds VEC floats to T (nearest even); 16-bit types convert two at a time
+// (one cvt.rn.{bf16x2,f16x2}.f32 per pair).
 template <typename T, int VEC>
 __device__ __forceinline__ Pack<T, VEC> pack(const float (&f)[VEC]) {
   Pack<T, VEC> pk;
+  if constexpr (sizeof(T) == 2 && VEC % 2 == 0) {
 #pragma unroll
-  for (int e = 0; e < VEC; ++e) pk.v[e] = from_f<T>(f[e]);
+    for (int e = 0; e < VEC; e += 2) {
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(f[e], f[e + 1]);
+        pk.v[e] = h.x;
+        pk.v[e + 1] = h.y;
+      } else {
+        const __half2 h = __floats2half2_rn(f[e], f[e + 1]);
+        pk.v[e] = h.x;
+        pk.v[e + 1] = h.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) pk.v[e] = from_f<T>(f[e]);
+  }
   return pk;
 }
 
@@ -157,6 +176,11 @@ int device_sm_count();  // SM count of the current device (cached per device)
 // Resident CTAs per SM for `func` at `block` threads and `smem` dynamic bytes
 // (cached per device and function).
 int occupancy(const void* func, int block, size_t smem);
+// Raises `func`'s dynamic shared-memory limit to `smem` bytes on the current
+// device (once per device and function).
+int prepare_smem(const void* func, size_t smem);
+// Device address of the library's fault word on the current device.
+unsigned int* fault_word();
 // Records `err` as the calling thread's last CUDA error and maps it to a status.
 int cuda_status(cudaError_t err);
 

@@ -2,46 +2,46 @@
 // by heads_f32.cu / heads_bf16.cu / heads_f16.cu.
 #pragma once
 
-#include "heads_impl.cuh"
+#include "heads_pipe.cuh"
 #include "rows_impl.cuh"
 
 namespace bloth {
 
-template <typename T, int D, bool NORM>
-int launch_head_fwd(const HeadArgs& a, cudaStream_t st) {
-  using G = HG<T, D>;
-  auto kern = head_fwd_kernel<T, D, NORM>;
-  const int occ = occupancy((const void*)kern, G::WPB * 32, 0);
+// CTAs of a launch over `ntok` tokens: one wave of resident CTAs, or fewer.
+template <typename T, int D, int MODE>
+int64_t head_pipe_grid(int64_t ntok) {
+  using P = HP<T, D, MODE>;
+  auto kern = head_pipe_kernel<T, D, MODE>;
+  if (prepare_smem((const void*)kern, P::SMEM) != BLOTH_OK) return -1;
+  const int occ = occupancy((const void*)kern, P::WPB * 32, P::SMEM);
   const int64_t wave = (int64_t)device_sm_count() * (occ > 0 ? occ : 1);
-  const int64_t need = ceil_div(a.B * a.S, G::WPB);
-  const int64_t grid = need < wave ? need : wave;
-  if (grid <= 0) return BLOTH_OK;
-  kern<<<(unsigned)grid, G::WPB * 32, 0, st>>>(a);
-  return cuda_status(cudaGetLastError());
+  const int64_t need = ceil_div(ntok, P::WPB);
+  return need < wave ? (need > 0 ? need : 0) : wave;
 }
 
-template <typename T, int D>
-int64_t head_bwd_grid(int64_t ntok) {
-  using G = HG<T, D>;
-  auto kern = head_bwd_kernel<T, D>;
-  const int occ = occupancy((const void*)kern, G::WPB * 32, 0);
-  const int64_t wave = (int64_t)device_sm_count() * (occ > 0 ? occ : 1);
-  const int64_t need = ceil_div(ntok, G::WPB);
-  return need < wave ? (need > 0 ? need : 0) : wave;
+template <typename T, int D, int MODE>
+int launch_head_fwd(const HeadArgs& a, cudaStream_t st) {
+  using P = HP<T, D, MODE>;
+  const int64_t grid = head_pipe_grid<T, D, MODE>(a.B * a.S);
+  if (grid < 0) return BLOTH_ERR_CUDA;
+  if (grid == 0) return BLOTH_OK;
+  head_pipe_kernel<T, D, MODE><<<(unsigned)grid, P::WPB * 32, P::SMEM, st>>>(a);
+  return cuda_status(cudaGetLastError());
 }
 
 template <typename T, int D>
 int launch_head_bwd(const HeadArgs& a0, void* ws, size_t ws_bytes, void* dw0, void* dw1,
                     cudaStream_t st) {
-  using G = HG<T, D>;
+  using P = HP<T, D, kHeadNormBwd>;
   using AccT = typename AccOf<T>::type;
-  const int64_t grid = head_bwd_grid<T, D>(a0.B * a0.S);
+  const int64_t grid = head_pipe_grid<T, D, kHeadNormBwd>(a0.B * a0.S);
+  if (grid < 0) return BLOTH_ERR_CUDA;
   if ((size_t)grid * 2 * D * sizeof(AccT) > ws_bytes || (grid > 0 && ws == nullptr))
     return BLOTH_ERR_WORKSPACE;
   if (grid > 0) {
     HeadArgs a = a0;
     a.partials = ws;
-    head_bwd_kernel<T, D><<<(unsigned)grid, G::WPB * 32, 0, st>>>(a);
+    head_pipe_kernel<T, D, kHeadNormBwd><<<(unsigned)grid, P::WPB * 32, P::SMEM, st>>>(a);
     const int rc = cuda_status(cudaGetLastError());
     if (rc != BLOTH_OK) return rc;
   }
@@ -64,7 +64,8 @@ int heads_fwd(const HeadArgs& a, int D, bool norm, cudaStream_t st) {
   int rc = BLOTH_ERR_SHAPE;
   dispatch_head_dim(D, [&](auto dd) {
     constexpr int DD = decltype(dd)::value;
-    rc = norm ? launch_head_fwd<T, DD, true>(a, st) : launch_head_fwd<T, DD, false>(a, st);
+    rc = norm ? launch_head_fwd<T, DD, kHeadNormFwd>(a, st)
+              : launch_head_fwd<T, DD, kHeadRopeFwd>(a, st);
   });
   return rc;
 }
@@ -86,7 +87,8 @@ size_t heads_bwd_workspace(int64_t ntok, int D) {
   size_t bytes = 0;
   dispatch_head_dim(D, [&](auto dd) {
     constexpr int DD = decltype(dd)::value;
-    bytes = (size_t)head_bwd_grid<T, DD>(ntok) * 2 * DD * sizeof(AccT);
+    const int64_t g = head_pipe_grid<T, DD, kHeadNormBwd>(ntok);
+    bytes = (size_t)(g > 0 ? g : 0) * 2 * DD * sizeof(AccT);
   });
   return bytes;
 }

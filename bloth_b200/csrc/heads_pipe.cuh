@@ -1,0 +1,429 @@
+// Pipelined per-head kernels: each warp streams its tokens' head rows
+// global -> shared with bulk copies through a private ring of NST slots, and
+// computes from shared memory.
+//
+// Work unit (chunk): up to R consecutive head rows of one tensor of one token,
+// R = 4 KiB / row bytes forward (16 rows at D = 128 bf16), 2 KiB / row bytes
+// backward (whose chunk also carries the forward input rows). A token is C0 chunks of q
+// then C1 chunks of k. Warp gw owns tokens gw, gw + W, gw + 2W, ... (W = warps
+// in the grid) and walks their chunks in order; before computing chunk g it
+// issues the copy of chunk g + NST - 1 into the slot that chunk g - 1 has just
+// released, so NST - 1 chunks (8 KiB per warp, 128 KiB per SM of 16 warps)
+// are in flight while one is computed. Lane 0 issues one bulk copy per chunk and
+// tensor when the token's heads are contiguous (head stride == D), else lanes
+// issue one copy per row. The backward chunk carries the output gradient
+// rows, the forward input rows and (when 16-byte aligned) the rows' rstd.
+//
+// cos/sin are derived once per token (see token_cos_sin) and the position of
+// the warp's next token is loaded one token ahead. Per-row math is that of the
+// reference's fused kernel (bloth/bloth/kernels/fused_norm_qkv_rope.py:59-92)
+// and its exact gradient; see heads_impl.cuh.
+#pragma once
+
+#include "bulk.cuh"
+#include "heads_impl.cuh"
+
+namespace bloth {
+
+enum HeadMode : int { kHeadNormFwd = 0, kHeadRopeFwd = 1, kHeadNormBwd = 2 };
+
+template <typename T, int D, int MODE>
+struct HP {
+  using G = HG<T, D>;
+  static constexpr bool BWD = MODE == kHeadNormBwd;
+  static constexpr int ROWB = D * (int)sizeof(T);            // bytes of one head row
+  static constexpr int R = (BWD ? 2048 : 4096) / ROWB;       // rows per chunk and tensor
+  static constexpr int NT = BWD ? 2 : 1;                     // tensors per chunk
+  static constexpr int RSTD_OFF = NT * R * ROWB;
+  static constexpr bool RSTD_BULK = BWD && (R % 4 == 0);     // rstd rows fill 16-byte units
+  static constexpr int SLOT = RSTD_OFF + (BWD ? ((R * 4 + 15) / 16) * 16 : 0);
+  static constexpr int NST = 3;                              // ring slots per warp
+  static constexpr int WPB = 16;                             // warps per CTA
+  static constexpr int RING = WPB * NST * SLOT;
+  static constexpr int SMEM = RING + WPB * NST * 8;          // + one mbarrier per slot
+  static_assert(R % G::RPW == 0, "chunk rows must fill whole warp steps");
+  static_assert(SLOT % 16 == 0, "bulk-copy destinations must be 16-byte aligned");
+  static_assert(SMEM <= 227 * 1024, "ring must fit in shared memory");
+};
+
+// Per-token rotation coefficients of one lane for one tensor (forward):
+// y = rstd * (x_own * alpha + x_partner * beta) with alpha = w_own * cos and
+// beta = -w_partner * sin in the first half, +w_partner * sin in the second
+// (y1 = n1*cos - n2*sin, y2 = n1*sin + n2*cos with n = x*rstd*w).
+template <typename T, int D>
+struct FwdCoef {
+  float al[HG<T, D>::VPL][HG<T, D>::VEC];
+  float be[HG<T, D>::VPL][HG<T, D>::VEC];
+};
+
+template <typename T, int D>
+__device__ __forceinline__ void make_fwd_coef(FwdCoef<T, D>& k,
+                                              const float (&wo)[HG<T, D>::VPL][HG<T, D>::VEC],
+                                              const float (&wp)[HG<T, D>::VPL][HG<T, D>::VEC],
+                                              const float (&cs)[HG<T, D>::VEC],
+                                              const float (&sn)[HG<T, D>::VEC], int li) {
+  using G = HG<T, D>;
+#pragma unroll
+  for (int j = 0; j < G::VPL; ++j) {
+    const bool first = slot_first<T, D>(j, li);
+#pragma unroll
+    for (int e = 0; e < G::VEC; ++e) {
+      k.al[j][e] = wo[j][e] * cs[e];
+      const float b = wp[j][e] * sn[e];
+      k.be[j][e] = first ? -b : b;
+    }
+  }
+}
+
+// One chunk of the forward: rows r0 .. r0+rc-1 of tensor TEN of token (b, s).
+template <typename T, int D, int MODE, int TEN>
+__device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned char* slot,
+                                               int64_t t, int64_t b, int64_t s, int r0, int rc,
+                                               const FwdCoef<T, D>& k, int rg, int li) {
+  using G = HG<T, D>;
+  using P = HP<T, D, MODE>;
+  constexpr bool NORM = MODE == kHeadNormFwd;
+  constexpr float kInvD = 1.0f / (float)D;  // exact: D is a power of two
+  const HT& dh = a.dst[TEN];
+  const int64_t dsh = dh.sh;
+  // lane's first element of its first row in this chunk
+  T* dptr = reinterpret_cast<T*>(const_cast<void*>(dh.p)) + b * dh.sb + s * dh.ss +
+            (int64_t)(r0 + rg) * dsh + slot_col<T, D>(0, li);
+  const unsigned char* sptr = slot + rg * P::ROWB + slot_col<T, D>(0, li) * (int)sizeof(T);
+  float* rstd_out = NORM ? a.rstd_out[TEN] + t * a.H[TEN] + r0 + rg : nullptr;
+#pragma unroll
+  for (int u = 0; u < P::R / G::RPW; ++u) {
+    if (u * G::RPW >= rc) break;  // partial chunk: no rows left in this step
+    const int rl = u * G::RPW + rg;
+    Pack<T, G::VEC> xp[G::VPL];
+#pragma unroll
+    for (int j = 0; j < G::VPL; ++j)
+      xp[j] = lds_pack<T, G::VEC>(sptr + u * G::RPW * P::ROWB +
+                                  j * G::LPR * G::VEC * (int)sizeof(T));
+    float xf[G::VPL][G::VEC], pf[G::VPL][G::VEC];
+#pragma unroll
+    for (int j = 0; j < G::VPL; ++j) unpack(xp[j], xf[j]);
+    partner<T, D>(xp, pf);
+    float rstd = 1.f;
+    if constexpr (NORM) {
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < G::VPL; ++j)
+#pragma unroll
+        for (int e = 0; e < G::VEC; e += 2) {
+          s0 = fmaf(xf[j][e], xf[j][e], s0);
+          s1 = fmaf(xf[j][e + 1], xf[j][e + 1], s1);
+        }
+      const float ss = group_lane_sum<G::LPR>(s0 + s1);
+      rstd = rsqrtf(fmaf(ss, kInvD, a.eps));
+    }
+    if (rl < rc) {
+      T* drow = dptr + (int64_t)(u * G::RPW) * dsh;
+#pragma unroll
+      for (int j = 0; j < G::VPL; ++j) {
+        float o[G::VEC];
+#pragma unroll
+        for (int e = 0; e < G::VEC; ++e)
+          o[e] = fmaf(xf[j][e], k.al[j][e], pf[j][e] * k.be[j][e]) * rstd;
+        stg_pack<T, G::VEC>(drow + j * G::LPR * G::VEC, pack<T, G::VEC>(o));
+      }
+      if constexpr (NORM) {
+        if (li == 0) rstd_out[u * G::RPW] = rstd;
+      }
+    }
+  }
+}
+
+// One chunk of the backward: dn = R^T dy = dy_own*cos + dy_partner*sn_signed
+// (sn_signed = +sin in the first half, -sin in the second), g = dn*w,
+// dx = rstd*(g - xhat*sum(g*xhat)/D), dweight += dn*xhat.
+template <typename T, int D, int TEN>
+__device__ __forceinline__ void pipe_bwd_chunk(
+    const HeadArgs& a, const unsigned char* slot, int64_t t, int64_t b, int64_t s, int r0,
+    int rc, const float (&wo)[HG<T, D>::VPL][HG<T, D>::VEC], const float (&cs)[HG<T, D>::VEC],
+    const float (&sp)[HG<T, D>::VPL][HG<T, D>::VEC],
+    typename AccOf<T>::type (&acc)[HG<T, D>::VPL][HG<T, D>::VEC], int rg, int li) {
+  using G = HG<T, D>;
+  using P = HP<T, D, kHeadNormBwd>;
+  constexpr float kInvD = 1.0f / (float)D;
+  const HT& dh = a.dst[TEN];
+  const int64_t dsh = dh.sh;
+  T* dptr = reinterpret_cast<T*>(const_cast<void*>(dh.p)) + b * dh.sb + s * dh.ss +
+            (int64_t)(r0 + rg) * dsh + slot_col<T, D>(0, li);
+  const unsigned char* gptr = slot + rg * P::ROWB + slot_col<T, D>(0, li) * (int)sizeof(T);
+  const unsigned char* xptr = gptr + P::R * P::ROWB;
+  const float* rstd_smem = reinterpret_cast<const float*>(slot + P::RSTD_OFF) + rg;
+  const float* rstd_src = a.rstd_in[TEN] + t * a.H[TEN] + r0 + rg;
+  const bool rstd_in_smem = P::RSTD_BULK && a.rstd_bulk;
+#pragma unroll
+  for (int u = 0; u < P::R / G::RPW; ++u) {
+    if (u * G::RPW >= rc) break;  // partial chunk: no rows left in this step
+    const int rl = u * G::RPW + rg;
+    const bool valid = rl < rc;
+    const float rstd = rstd_in_smem ? rstd_smem[u * G::RPW]
+                                    : (valid ? __ldg(rstd_src + u * G::RPW) : 0.f);
+    Pack<T, G::VEC> gp[G::VPL], xp[G::VPL];
+#pragma unroll
+    for (int j = 0; j < G::VPL; ++j) {
+      const int off = u * G::RPW * P::ROWB + j * G::LPR * G::VEC * (int)sizeof(T);
+      gp[j] = lds_pack<T, G::VEC>(gptr + off);
+      xp[j] = lds_pack<T, G::VEC>(xptr + off);
+    }
+    float gf[G::VPL][G::VEC], pf[G::VPL][G::VEC];
+#pragma unroll
+    for (int j = 0; j < G::VPL; ++j) unpack(gp[j], gf[j]);
+    partner<T, D>(gp, pf);
+    float g[G::VPL][G::VEC], xh[G::VPL][G::VEC];
+    float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < G::VPL; ++j) {
+      float xf[G::VEC];
+      unpack(xp[j], xf);
+#pragma unroll
+      for (int e = 0; e < G::VEC; ++e) {
+        const float dn = fmaf(pf[j][e], sp[j][e], gf[j][e] * cs[e]);
+        xh[j][e] = xf[e] * rstd;
+        g[j][e] = dn * wo[j][e];
+        if (e & 1) d1 = fmaf(g[j][e], xh[j][e], d1);
+        else d0 = fmaf(g[j][e], xh[j][e], d0);
+        if (valid) acc_add(acc[j][e], dn, xh[j][e]);
+      }
+    }
+    const float dot = group_lane_sum<G::LPR>(d0 + d1) * kInvD;
+    if (valid) {
+      T* drow = dptr + (int64_t)(u * G::RPW) * dsh;
+#pragma unroll
+      for (int j = 0; j < G::VPL; ++j) {
+        float o[G::VEC];
+#pragma unroll
+        for (int e = 0; e < G::VEC; ++e) o[e] = rstd * fmaf(-xh[j][e], dot, g[j][e]);
+        stg_pack<T, G::VEC>(drow + j * G::LPR * G::VEC, pack<T, G::VEC>(o));
+      }
+    }
+  }
+}
+
+// Position of a warp in its chunk sequence: token t = (b, s), chunk j of the
+// token's CT chunks, `left` chunks still to go. Advanced without divisions in
+// the common case (one 32-bit division when a step crosses a sequence).
+struct ChunkCursor {
+  int64_t t, b, s;
+  int j;
+  int64_t left;
+  __device__ __forceinline__ void next(int CT, int64_t W, int64_t S) {
+    --left;
+    if (++j == CT) {
+      j = 0;
+      t += W;
+      s += W;
+      if (s >= S) {
+        const uint32_t q = (uint32_t)((uint64_t)s / (uint64_t)S);
+        b += q;
+        s -= (int64_t)q * S;
+      }
+    }
+  }
+};
+
+template <typename T, int D, int MODE>
+__global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
+    head_pipe_kernel(const HeadArgs a) {
+  using G = HG<T, D>;
+  using P = HP<T, D, MODE>;
+  using AccT = typename AccOf<T>::type;
+  constexpr bool BWD = MODE == kHeadNormBwd;
+  constexpr bool NORM = MODE != kHeadRopeFwd;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int rg = lane / G::LPR;
+  const int li = lane % G::LPR;
+  const int pg = G::VPL == 1 ? li % (G::LPR / 2) : li;
+  unsigned char* ring = smem + warp * P::NST * P::SLOT;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::RING) + warp * P::NST;
+  if (lane == 0) {
+#pragma unroll
+    for (int q = 0; q < P::NST; ++q) mbar_init(&bars[q], 1);
+    mbar_init_fence();
+  }
+  __syncwarp();
+
+  float invf[G::APL];
+#pragma unroll
+  for (int q = 0; q < G::APL; ++q)
+    invf[q] = a.inv_freq ? __ldg(a.inv_freq + lane * G::APL + q) : 0.f;
+
+  // Weights of the lane's columns (and, forward, of their partner columns).
+  float wo[2][G::VPL][G::VEC], wp[2][G::VPL][G::VEC];
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int j = 0; j < G::VPL; ++j) {
+      if (NORM && a.H[q] != 0) {
+        const int c = slot_col<T, D>(j, li);
+        ld_any_vec<G::VEC>(a.w[q], c, a.w_dt, true, wo[q][j]);
+        if constexpr (!BWD) {
+          const int pc = c < G::HALF ? c + G::HALF : c - G::HALF;
+          ld_any_vec<G::VEC>(a.w[q], pc, a.w_dt, true, wp[q][j]);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < G::VEC; ++e) wo[q][j][e] = 1.f;
+      }
+      if (BWD || !NORM || a.H[q] == 0)
+#pragma unroll
+        for (int e = 0; e < G::VEC; ++e) wp[q][j][e] = 1.f;
+    }
+  AccT acc[2][G::VPL][G::VEC];
+#pragma unroll
+  for (int q = 0; q < 2; ++q)
+#pragma unroll
+    for (int j = 0; j < G::VPL; ++j)
+#pragma unroll
+      for (int e = 0; e < G::VEC; ++e) acc[q][j][e] = AccT(0);
+
+  const int C0 = (a.H[0] + P::R - 1) / P::R;
+  const int C1 = (a.H[1] + P::R - 1) / P::R;
+  const int CT = C0 + C1;
+  const int64_t ntok = a.B * a.S;
+  const int64_t W = (int64_t)gridDim.x * P::WPB;
+  const int64_t gw = (int64_t)blockIdx.x * P::WPB + warp;
+  const int64_t my_tok = gw < ntok ? (ntok - 1 - gw) / W + 1 : 0;
+  const int64_t nchunk = my_tok * CT;
+
+  // Issues chunk `c` into ring slot `sl`.
+  auto issue = [&](const ChunkCursor& c, int sl) {
+    const int ten = c.j < C0 ? 0 : 1;
+    const int r0 = (ten == 0 ? c.j : c.j - C0) * P::R;
+    const int rc = min(P::R, a.H[ten] - r0);
+    unsigned char* dst = ring + sl * P::SLOT;
+    uint64_t* bar = &bars[sl];
+    const bool rstd_copy = P::RSTD_BULK && a.rstd_bulk;
+    const uint32_t bytes = (uint32_t)(rc * P::ROWB * P::NT) + (rstd_copy ? (uint32_t)rc * 4u : 0u);
+    if (lane == 0) mbar_arrive_expect_tx(bar, bytes);
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < P::NT; ++q) {
+      const HT& h = q == 0 ? a.src[ten] : a.x[ten];
+      const T* base =
+          reinterpret_cast<const T*>(h.p) + c.b * h.sb + c.s * h.ss + (int64_t)r0 * h.sh;
+      unsigned char* d = dst + q * P::R * P::ROWB;
+      if (h.sh == D) {
+        if (lane == 0) bulk_load(d, base, (uint32_t)(rc * P::ROWB), bar);
+      } else if (lane < rc) {
+        bulk_load(d + lane * P::ROWB, base + (int64_t)lane * h.sh, (uint32_t)P::ROWB, bar);
+      }
+    }
+    if (rstd_copy && lane == 0)
+      bulk_load(dst + P::RSTD_OFF, a.rstd_in[ten] + c.t * a.H[ten] + r0, (uint32_t)rc * 4u, bar);
+  };
+
+  ChunkCursor cc;
+  cc.t = gw;
+  cc.b = my_tok > 0 ? gw / a.S : 0;
+  cc.s = gw - cc.b * a.S;
+  cc.j = 0;
+  cc.left = nchunk;
+  ChunkCursor ic = cc;  // issue cursor, NST - 1 chunks ahead
+  int isl = 0;
+  for (int q = 0; q < P::NST - 1 && ic.left > 0; ++q) {
+    issue(ic, isl);
+    ic.next(CT, W, a.S);
+    isl = isl + 1 == P::NST ? 0 : isl + 1;
+  }
+
+  float cs[G::VEC], sn[G::VEC];
+  FwdCoef<T, D> kq, kk;            // forward coefficients of q and k for the current token
+  float sp[G::VPL][G::VEC];        // backward: signed sin per slot
+  int64_t pos_next = my_tok > 0 ? token_pos<T, D>(a, cc.b, cc.s) : 0;
+  const float sgn = a.transpose ? -1.f : 1.f;
+  int csl = 0;
+  uint32_t cph = 0;
+  while (cc.left > 0) {
+    if (ic.left > 0) {
+      issue(ic, isl);
+      ic.next(CT, W, a.S);
+      isl = isl + 1 == P::NST ? 0 : isl + 1;
+    }
+    if (cc.j == 0) {
+      const int64_t p = pos_next;
+      if (cc.left > CT) {  // the warp has another token: load its position now
+        int64_t s2 = cc.s + W, b2 = cc.b;
+        if (s2 >= a.S) {
+          const uint32_t q = (uint32_t)((uint64_t)s2 / (uint64_t)a.S);
+          b2 += q;
+          s2 -= (int64_t)q * a.S;
+        }
+        pos_next = token_pos<T, D>(a, b2, s2);
+      }
+      token_cos_sin<T, D>(a, cc.b, p, lane, pg, invf, cs, sn);
+      if constexpr (MODE == kHeadRopeFwd) {
+#pragma unroll
+        for (int e = 0; e < G::VEC; ++e) sn[e] *= sgn;
+      }
+      if constexpr (BWD) {
+#pragma unroll
+        for (int jj = 0; jj < G::VPL; ++jj) {
+          const bool first = slot_first<T, D>(jj, li);
+#pragma unroll
+          for (int e = 0; e < G::VEC; ++e) sp[jj][e] = first ? sn[e] : -sn[e];
+        }
+      } else {
+        make_fwd_coef<T, D>(kq, wo[0], wp[0], cs, sn, li);
+        if (C1 > 0) make_fwd_coef<T, D>(kk, wo[1], wp[1], cs, sn, li);
+      }
+    }
+    const int ten = cc.j < C0 ? 0 : 1;
+    const int r0 = (ten == 0 ? cc.j : cc.j - C0) * P::R;
+    const int rc = min(P::R, a.H[ten] - r0);
+    const bool landed = mbar_wait(&bars[csl], cph, a.fault);
+    if (!__all_sync(0xffffffffu, landed)) break;
+    const unsigned char* slot = ring + csl * P::SLOT;
+    if constexpr (BWD) {
+      if (ten == 0)
+        pipe_bwd_chunk<T, D, 0>(a, slot, cc.t, cc.b, cc.s, r0, rc, wo[0], cs, sp, acc[0], rg, li);
+      else
+        pipe_bwd_chunk<T, D, 1>(a, slot, cc.t, cc.b, cc.s, r0, rc, wo[1], cs, sp, acc[1], rg, li);
+    } else {
+      if (ten == 0) pipe_fwd_chunk<T, D, MODE, 0>(a, slot, cc.t, cc.b, cc.s, r0, rc, kq, rg, li);
+      else pipe_fwd_chunk<T, D, MODE, 1>(a, slot, cc.t, cc.b, cc.s, r0, rc, kk, rg, li);
+    }
+    // release the slot: order this lane's reads before the next bulk write
+    fence_proxy_async_smem();
+    __syncwarp();
+    cc.next(CT, W, a.S);
+    if (++csl == P::NST) {
+      csl = 0;
+      cph ^= 1u;
+    }
+  }
+
+  if constexpr (BWD) {
+    // Weight-gradient partials: fold the row groups of each warp (lanes with
+    // equal li), then the warps of the CTA in a fixed order, through the
+    // (now idle) ring memory.
+    __syncthreads();
+    AccT* red = reinterpret_cast<AccT*>(smem);  // [WPB][2*D]
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+#pragma unroll
+      for (int j = 0; j < G::VPL; ++j)
+#pragma unroll
+        for (int e = 0; e < G::VEC; ++e) {
+#pragma unroll
+          for (int o = G::LPR; o < 32; o <<= 1)
+            acc[q][j][e] += __shfl_xor_sync(0xffffffffu, acc[q][j][e], o);
+          if (rg == 0) red[warp * 2 * D + q * D + slot_col<T, D>(j, li) + e] = acc[q][j][e];
+        }
+    __syncthreads();
+    AccT* part = reinterpret_cast<AccT*>(a.partials) + (int64_t)blockIdx.x * 2 * D;
+    for (int c = threadIdx.x; c < 2 * D; c += P::WPB * 32) {
+      AccT sum = AccT(0);
+#pragma unroll
+      for (int wi = 0; wi < P::WPB; ++wi) sum += red[wi * 2 * D + c];
+      part[c] = sum;
+    }
+  }
+}
+
+}  // namespace bloth

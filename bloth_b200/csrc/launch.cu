@@ -2,12 +2,18 @@
 // caches, CUDA error capture) and the deterministic weight-gradient reduce.
 #include <map>
 #include <mutex>
+#include <set>
 #include <tuple>
 
+#include "bulk.cuh"
 #include "common.cuh"
 #include "rows_impl.cuh"
 
 namespace bloth {
+
+// Fault bits recorded by kernels that gave up a bounded wait (kFault*).
+// Kernels in other translation units receive its address as an argument.
+__device__ unsigned int g_device_fault = 0;
 
 static thread_local int g_last_cuda_error = 0;
 
@@ -66,6 +72,52 @@ int occupancy(const void* func, int block, size_t smem) {
   std::lock_guard<std::mutex> lk(mu);
   cache[key] = n;
   return n;
+}
+
+int prepare_smem(const void* func, size_t smem) {
+  using Key = std::tuple<int, const void*, size_t>;
+  static std::mutex mu;
+  static std::set<Key> done;
+  const int dev = current_device();
+  const Key key{dev, func, smem};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count(key)) return BLOTH_OK;
+  }
+  const cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return cuda_status(e);
+  std::lock_guard<std::mutex> lk(mu);
+  done.insert(key);
+  return BLOTH_OK;
+}
+
+unsigned int* fault_word() {
+  static std::mutex mu;
+  static std::map<int, unsigned int*> cache;
+  const int dev = current_device();
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  void* p = nullptr;
+  if (dev < 0 || cudaGetSymbolAddress(&p, g_device_fault) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  cache[dev] = static_cast<unsigned int*>(p);
+  return static_cast<unsigned int*>(p);
+}
+
+int device_fault(int reset) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_device_fault, sizeof(v));
+  if (e != cudaSuccess) return -cuda_status(e);
+  if (reset) {
+    const unsigned int z = 0;
+    e = cudaMemcpyToSymbol(g_device_fault, &z, sizeof(z));
+    if (e != cudaSuccess) return -cuda_status(e);
+  }
+  return (int)v;
 }
 
 // Column sums of P accumulator rows of N: CTA x handles 32 columns; warp wi

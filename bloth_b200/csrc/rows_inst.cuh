@@ -3,7 +3,7 @@
 // for its type, so the kernel variants compile in parallel.
 #pragma once
 
-#include "rows_impl.cuh"
+#include "rows_pipe.cuh"
 
 namespace bloth {
 
@@ -40,6 +40,75 @@ int launch_row_bwd(const RowArgs& a0, void* ws, size_t ws_bytes, void* dw, cudaS
                                 a0.w_dt, st);
 }
 
+// Shared-memory plan of the pipelined row kernels for rows of N: ring slots,
+// whether the fp32 weight copy is staged, within a per-CTA budget that leaves
+// room for several CTAs per SM (72 KB for 128-thread CTAs, 112 KB for 256,
+// 200 KB for larger). nst == 0 when even two slots do not fit (the register
+// kernels then take the rows).
+template <typename T, typename PC, bool BWD>
+RowPipe pipe_plan(int N, bool contiguous) {
+  RowPipe pp;
+  pp.row_bytes = N * (int)sizeof(T);
+  pp.slot_bytes = PC::RPC * pp.row_bytes * (BWD ? 2 : 1);
+  pp.contiguous = contiguous ? 1 : 0;
+  pp.fault = fault_word();
+  const size_t budget = PC::BLOCK <= 128 ? 72 * 1024 : (PC::BLOCK <= 256 ? 112 * 1024 : 200 * 1024);
+  const size_t slot = (size_t)pp.slot_bytes + 8;
+  const size_t wbytes = (size_t)N * 4;
+  pp.w_staged = wbytes <= 32 * 1024 && budget >= wbytes + 2 * slot ? 1 : 0;
+  const size_t avail = budget - (pp.w_staged ? wbytes : 0);
+  const size_t n = avail / slot;
+  pp.nst = n >= 4 ? 4 : (n >= 2 ? (int)n : 0);
+  return pp;
+}
+
+inline size_t pipe_smem(const RowPipe& pp, int N) {
+  return (size_t)pp.nst * (pp.slot_bytes + 8) + (pp.w_staged ? (size_t)N * 4 : 0);
+}
+
+// Grid of the pipelined kernel (one wave of resident CTAs or fewer), or -1 if
+// the kernel cannot be prepared on this device.
+template <typename T, int VEC, typename PC, bool ROPE, bool BWD>
+int64_t row_pipe_grid(int64_t M, int N, const RowPipe& pp) {
+  auto kern = row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, ROPE, BWD>;
+  const size_t smem = pipe_smem(pp, N);
+  if (prepare_smem((const void*)kern, smem) != BLOTH_OK) return -1;
+  const int occ = occupancy((const void*)kern, PC::BLOCK, smem);
+  const int64_t wave = (int64_t)device_sm_count() * (occ > 0 ? occ : 1);
+  const int64_t need = ceil_div(M, PC::RPC);
+  return need < wave ? (need > 0 ? need : 0) : wave;
+}
+
+template <typename T, int VEC, typename PC, bool ROPE>
+int launch_row_pipe_fwd(const RowArgs& a, const RowPipe& pp, cudaStream_t st) {
+  const int64_t grid = row_pipe_grid<T, VEC, PC, ROPE, false>(a.M, a.N, pp);
+  if (grid < 0) return BLOTH_ERR_CUDA;
+  if (grid == 0) return BLOTH_OK;
+  row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, ROPE, false>
+      <<<(unsigned)grid, PC::BLOCK, pipe_smem(pp, a.N), st>>>(a, pp);
+  return cuda_status(cudaGetLastError());
+}
+
+template <typename T, int VEC, typename PC, bool ROPE>
+int launch_row_pipe_bwd(const RowArgs& a0, const RowPipe& pp, void* ws, size_t ws_bytes, void* dw,
+                        cudaStream_t st) {
+  using AccT = typename AccOf<T>::type;
+  const int64_t grid = row_pipe_grid<T, VEC, PC, ROPE, true>(a0.M, a0.N, pp);
+  if (grid < 0) return BLOTH_ERR_CUDA;
+  if ((size_t)grid * a0.N * sizeof(AccT) > ws_bytes || (grid > 0 && ws == nullptr))
+    return BLOTH_ERR_WORKSPACE;
+  if (grid > 0) {
+    RowArgs a = a0;
+    a.partials = ws;
+    row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, ROPE, true>
+        <<<(unsigned)grid, PC::BLOCK, pipe_smem(pp, a0.N), st>>>(a, pp);
+    const int rc = cuda_status(cudaGetLastError());
+    if (rc != BLOTH_OK) return rc;
+  }
+  return launch_dw_reduce<AccT>(reinterpret_cast<const AccT*>(ws), grid, a0.N, dw, a0.N, nullptr,
+                                a0.w_dt, st);
+}
+
 template <typename T>
 int rows_fwd(const RowArgs& a, bool rope, bool vec, cudaStream_t st) {
   constexpr int V = 16 / sizeof(T);
@@ -49,10 +118,20 @@ int rows_fwd(const RowArgs& a, bool rope, bool vec, cudaStream_t st) {
     constexpr int VV = decltype(vecc)::value;
     rc = rope ? launch_row_fwd<T, VV, C, true>(a, st) : launch_row_fwd<T, VV, C, false>(a, st);
   };
-  if (vec)
-    dispatch_row_cfg<V>(a.N, [&](auto cfg) { go(cfg, std::integral_constant<int, V>{}); });
-  else
+  if (vec) {
+    dispatch_row_cfg<V>(a.N, [&](auto cfg) {
+      using C = decltype(cfg);
+      using PC = PipeCfg<C::TPR, C::VPT>;
+      const RowPipe pp = pipe_plan<T, PC, false>(a.N, a.ldx == a.N);
+      if (pp.nst > 0)
+        rc = rope ? launch_row_pipe_fwd<T, V, PC, true>(a, pp, st)
+                  : launch_row_pipe_fwd<T, V, PC, false>(a, pp, st);
+      else
+        go(cfg, std::integral_constant<int, V>{});
+    });
+  } else {
     dispatch_row_cfg<1>(a.N, [&](auto cfg) { go(cfg, std::integral_constant<int, 1>{}); });
+  }
   return rc;
 }
 
@@ -67,15 +146,25 @@ int rows_bwd(const RowArgs& a, bool rope, bool vec, void* ws, size_t ws_bytes, v
     rc = rope ? launch_row_bwd<T, VV, C, true>(a, ws, ws_bytes, dw, st)
               : launch_row_bwd<T, VV, C, false>(a, ws, ws_bytes, dw, st);
   };
-  if (vec)
-    dispatch_row_cfg<V>(a.N, [&](auto cfg) { go(cfg, std::integral_constant<int, V>{}); });
-  else
+  if (vec) {
+    dispatch_row_cfg<V>(a.N, [&](auto cfg) {
+      using C = decltype(cfg);
+      using PC = PipeCfg<C::TPR, C::VPT>;
+      const RowPipe pp = pipe_plan<T, PC, true>(a.N, a.ldx == a.N && a.lddy == a.N);
+      if (pp.nst > 0)
+        rc = rope ? launch_row_pipe_bwd<T, V, PC, true>(a, pp, ws, ws_bytes, dw, st)
+                  : launch_row_pipe_bwd<T, V, PC, false>(a, pp, ws, ws_bytes, dw, st);
+      else
+        go(cfg, std::integral_constant<int, V>{});
+    });
+  } else {
     dispatch_row_cfg<1>(a.N, [&](auto cfg) { go(cfg, std::integral_constant<int, 1>{}); });
+  }
   return rc;
 }
 
-// Workspace for the backward: the larger of the vector and scalar paths'
-// needs, so the size does not depend on the pointers' alignment.
+// Workspace for the backward: the largest need of the pipelined, vector and
+// scalar paths, so the size does not depend on the pointers' alignment.
 template <typename T>
 size_t rows_bwd_workspace(int64_t M, int N, bool rope) {
   using AccT = typename AccOf<T>::type;
@@ -87,7 +176,19 @@ size_t rows_bwd_workspace(int64_t M, int N, bool rope) {
     const int64_t g = rope ? row_bwd_grid<T, VV, C, true>(M) : row_bwd_grid<T, VV, C, false>(M);
     if (g > grid) grid = g;
   };
-  dispatch_row_cfg<V>(N, [&](auto cfg) { take(cfg, std::integral_constant<int, V>{}); });
+  dispatch_row_cfg<V>(N, [&](auto cfg) {
+    take(cfg, std::integral_constant<int, V>{});
+    using C = decltype(cfg);
+    using PC = PipeCfg<C::TPR, C::VPT>;
+    if (N % V == 0) {
+      const RowPipe pp = pipe_plan<T, PC, true>(N, true);
+      if (pp.nst > 0) {
+        const int64_t g = rope ? row_pipe_grid<T, V, PC, true, true>(M, N, pp)
+                               : row_pipe_grid<T, V, PC, false, true>(M, N, pp);
+        if (g > grid) grid = g;
+      }
+    }
+  });
   dispatch_row_cfg<1>(N, [&](auto cfg) { take(cfg, std::integral_constant<int, 1>{}); });
   return (size_t)grid * (size_t)N * sizeof(AccT);
 }

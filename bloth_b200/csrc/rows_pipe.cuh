@@ -1,0 +1,351 @@
+// Pipelined row kernels: RMSNorm (optionally + table RoPE) over rows of N,
+// forward and backward, with the rows staged global -> shared by bulk copies.
+//
+// A CTA of RPC row groups x TPR threads (same thread -> column map as the
+// register kernels in rows_impl.cuh) walks blocks of RPC consecutive rows
+// with a grid stride. Block i lands in ring slot i % NST; thread 0 issues the
+// copy of block i + NST - 1 (one bulk copy of the whole block when the rows
+// are contiguous, else one per row from the lanes of warp 0) before the CTA
+// waits for block i, so NST - 1 blocks are in flight while one is computed.
+// A slot holds the block's x rows (forward) or dy rows then x rows
+// (backward); NST and the slot size are chosen on the host from N so that a
+// CTA uses at most ~200 KB of shared memory. The trailing __syncthreads of an
+// iteration releases its slot.
+//
+// Math: as rows_impl.cuh (reference bloth/bloth/kernels/rms_norm.py:59-111,
+// fused_norm_qkv_rope.py:59-96); the RoPE partner half is read from the
+// staged row in shared memory.
+#pragma once
+
+#include "bulk.cuh"
+#include "rows_impl.cuh"
+
+namespace bloth {
+
+struct RowPipe {
+  int nst;           // ring slots
+  int row_bytes;     // N * sizeof(T), a multiple of 16
+  int slot_bytes;    // RPC * row_bytes * (1 forward, 2 backward)
+  int contiguous;    // rows of a block are adjacent in memory (ld == N) for every input
+  int w_staged;      // the weight is converted to fp32 into shared memory once per CTA
+  unsigned int* fault;
+};
+
+// CTA shape of the pipelined kernels: TPR threads per row and VPT vectors per
+// thread as the register kernels, but RPC = 128 / TPR rows per block (one
+// row for wide rows), so a CTA is 128 threads or one row group, and several
+// CTAs share an SM.
+template <int TPR_, int VPT_>
+struct PipeCfg {
+  static constexpr int TPR = TPR_;
+  static constexpr int VPT = VPT_;
+  static constexpr int RPC = TPR >= 128 ? 1 : 128 / TPR;
+  static constexpr int BLOCK = TPR * RPC;
+  static constexpr int MIN_BLOCKS = BLOCK >= 512 ? 1 : 512 / BLOCK;
+};
+
+// Weight values for columns c..c+VEC-1: from the fp32 copy in shared memory
+// when staged, else from global memory.
+template <int VEC>
+__device__ __forceinline__ void row_weight(const float* ws, const RowArgs& a, int c, bool wv,
+                                           float (&w)[VEC]) {
+  if (ws != nullptr) {
+#pragma unroll
+    for (int q = 0; q < VEC; q += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(ws + c + q);
+      w[q] = v.x;
+      w[q + 1] = v.y;
+      w[q + 2] = v.z;
+      w[q + 3] = v.w;
+    }
+  } else {
+    ld_any_vec<VEC>(a.w, c, a.w_dt, wv, w);
+  }
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsigned char* rowp,
+                                              float rstd, const RowArgs& a, int64_t row) {
+  const int64_t h = a.half;
+  if (c >= 2 * h) return;
+  if (a.cs_vec && (h % VEC) == 0) {
+    const bool first = c < h;
+    const int64_t pc = first ? c + h : c - h;
+    const int64_t i = first ? c : c - h;
+    float xp[VEC], wp[VEC], cs[VEC], sn[VEC];
+    unpack(lds_pack<T, VEC>(rowp + pc * (int64_t)sizeof(T)), xp);
+    ld_any_vec<VEC>(a.w, pc, a.w_dt, a.w_vec, wp);
+    ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, true, cs);
+    ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, true, sn);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const float np = xp[e] * rstd * wp[e];
+      o[e] = first ? (o[e] * cs[e] - np * sn[e]) : (np * sn[e] + o[e] * cs[e]);
+    }
+  } else {
+    const T* xr = reinterpret_cast<const T*>(rowp);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const int64_t cc = c + e;
+      if (cc < 2 * h && cc < a.N) {
+        const bool first = cc < h;
+        const int64_t pc = first ? cc + h : cc - h;
+        const int64_t i = first ? cc : cc - h;
+        const float np = to_f(xr[pc]) * rstd * ld_any(a.w, pc, a.w_dt);
+        const float cs = ld_any(a.cos, row * a.ldcs + i, a.cs_dt);
+        const float sn = ld_any(a.sin, row * a.ldcs + i, a.cs_dt);
+        o[e] = first ? (o[e] * cs - np * sn) : (np * sn + o[e] * cs);
+      }
+    }
+  }
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsigned char* dyp,
+                                              const RowArgs& a, int64_t row) {
+  const int64_t h = a.half;
+  if (c >= 2 * h) return;
+  if (a.cs_vec && (h % VEC) == 0) {
+    const bool first = c < h;
+    const int64_t pc = first ? c + h : c - h;
+    const int64_t i = first ? c : c - h;
+    float dp[VEC], cs[VEC], sn[VEC];
+    unpack(lds_pack<T, VEC>(dyp + pc * (int64_t)sizeof(T)), dp);
+    ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, true, cs);
+    ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, true, sn);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e)
+      d[e] = first ? (d[e] * cs[e] + dp[e] * sn[e]) : (d[e] * cs[e] - dp[e] * sn[e]);
+  } else {
+    const T* dr = reinterpret_cast<const T*>(dyp);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) {
+      const int64_t cc = c + e;
+      if (cc < 2 * h && cc < a.N) {
+        const bool first = cc < h;
+        const int64_t pc = first ? cc + h : cc - h;
+        const int64_t i = first ? cc : cc - h;
+        const float dp = to_f(dr[pc]);
+        const float cs = ld_any(a.cos, row * a.ldcs + i, a.cs_dt);
+        const float sn = ld_any(a.sin, row * a.ldcs + i, a.cs_dt);
+        d[e] = first ? (d[e] * cs + dp * sn) : (d[e] * cs - dp * sn);
+      }
+    }
+  }
+}
+
+template <typename T, int VEC, int TPR, int VPT, int RPC, bool ROPE, bool BWD>
+__global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 512 ? 1 : 512 / (TPR * RPC))
+    row_pipe_kernel(const RowArgs a, const RowPipe pp) {
+  using RR = RowReduce<TPR, RPC>;
+  using AccT = typename AccOf<T>::type;
+  __shared__ float red[RR::SMEM_FLOATS];
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int grp = threadIdx.x / TPR;
+  const int lt = threadIdx.x % TPR;
+  const int N = a.N;
+  const float inv_n = 1.0f / (float)N;
+  const bool wv = a.w_vec != 0;
+  const int NST = pp.nst;
+  float* ws = pp.w_staged ? reinterpret_cast<float*>(smem + (size_t)NST * pp.slot_bytes) : nullptr;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * pp.slot_bytes +
+                                               (pp.w_staged ? (size_t)N * 4 : 0));
+  if (threadIdx.x == 0) {
+    for (int q = 0; q < NST; ++q) mbar_init(&bars[q], 1);
+    mbar_init_fence();
+  }
+  if (ws != nullptr)
+    for (int c = threadIdx.x; c < N; c += TPR * RPC) ws[c] = ld_any(a.w, c, a.w_dt);
+  __syncthreads();
+
+  const int64_t nblk = (a.M + RPC - 1) / RPC;
+  const int64_t my_blk = blockIdx.x < nblk ? (nblk - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+  // Thread 0 (with the lanes of warp 0 for per-row copies) issues block i
+  // into ring slot sl.
+  auto issue = [&](int64_t i, int sl) {
+    if (i >= my_blk || threadIdx.x >= 32) return;
+    const int64_t row0 = ((int64_t)blockIdx.x + i * gridDim.x) * RPC;
+    const int nrow = (int)min((int64_t)RPC, a.M - row0);
+    unsigned char* dst = smem + (size_t)sl * pp.slot_bytes;
+    uint64_t* bar = &bars[sl];
+    constexpr int NTEN = BWD ? 2 : 1;
+    if (threadIdx.x == 0)
+      mbar_arrive_expect_tx(bar, (uint32_t)(nrow * pp.row_bytes * NTEN));
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < NTEN; ++q) {
+      const T* src = reinterpret_cast<const T*>(BWD && q == 0 ? a.dy : a.x);
+      const int64_t ld = BWD && q == 0 ? a.lddy : a.ldx;
+      unsigned char* d = dst + (size_t)q * RPC * pp.row_bytes;
+      if (pp.contiguous) {
+        if (threadIdx.x == 0)
+          bulk_load(d, src + row0 * ld, (uint32_t)(nrow * pp.row_bytes), bar);
+      } else if ((int)threadIdx.x < nrow) {
+        bulk_load(d + (size_t)threadIdx.x * pp.row_bytes, src + (row0 + threadIdx.x) * ld,
+                  (uint32_t)pp.row_bytes, bar);
+      }
+    }
+  };
+
+  for (int q = 0; q < NST - 1; ++q) issue(q, q);
+  int isl = NST - 1;  // slot of the next block to issue
+  int csl = 0;        // slot of the block being computed, and its phase
+  uint32_t cph = 0;
+
+  AccT acc[VPT][VEC];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j)
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[j][e] = AccT(0);
+
+  int parity = 0;
+  float rstd_next = 0.f;
+  if (BWD && my_blk > 0) {
+    const int64_t r = (int64_t)blockIdx.x * RPC + grp;
+    rstd_next = r < a.M ? __ldg(a.rstd_in + r) : 0.f;
+  }
+  for (int64_t i = 0; i < my_blk; ++i, parity ^= 1) {
+    issue(i + NST - 1, isl);
+    isl = isl + 1 == NST ? 0 : isl + 1;
+    const int64_t row = ((int64_t)blockIdx.x + i * gridDim.x) * RPC + grp;
+    const bool valid = row < a.M;
+    float rstd_in = 0.f;
+    if constexpr (BWD) {
+      rstd_in = rstd_next;
+      const int64_t r2 = row + (int64_t)gridDim.x * RPC;
+      if (i + 1 < my_blk && r2 < a.M) rstd_next = __ldg(a.rstd_in + r2);
+    }
+    const bool landed = mbar_wait(&bars[csl], cph, pp.fault);
+    if (!__syncthreads_and(landed)) break;
+    const unsigned char* slot = smem + (size_t)csl * pp.slot_bytes;
+    if (++csl == NST) {
+      csl = 0;
+      cph ^= 1u;
+    }
+    if constexpr (!BWD) {
+      const unsigned char* rowp = slot + (size_t)grp * pp.row_bytes;
+      Pack<T, VEC> xp[VPT];
+      float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int c = (j * TPR + lt) * VEC;
+        if (valid && c < N) {
+          xp[j] = lds_pack<T, VEC>(rowp + (int64_t)c * sizeof(T));
+        } else {
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) xp[j].v[e] = from_f<T>(0.f);
+        }
+        float f[VEC];
+        unpack(xp[j], f);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) {
+          if (e & 1) s1 = fmaf(f[e], f[e], s1);
+          else s0 = fmaf(f[e], f[e], s0);
+        }
+      }
+      const float ss = RR::sum(s0 + s1, red, grp, lt, parity);
+      const float rstd = rsqrtf(ss * inv_n + a.eps);
+      if (valid) {
+        if (lt == 0) a.rstd_out[row] = rstd;
+        T* yr = reinterpret_cast<T*>(a.out) + row * a.ldo;
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          const int c = (j * TPR + lt) * VEC;
+          if (c < N) {
+            float f[VEC], w[VEC];
+            unpack(xp[j], f);
+            row_weight<VEC>(ws, a, c, wv, w);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) f[e] = f[e] * rstd * w[e];
+            if constexpr (ROPE) rope_pipe_fwd<T, VEC>(f, c, rowp, rstd, a, row);
+            stg_pack<T, VEC>(yr + c, pack<T, VEC>(f));
+          }
+        }
+      }
+    } else {
+      const unsigned char* dyp = slot + (size_t)grp * pp.row_bytes;
+      const unsigned char* xrp = slot + (size_t)(RPC + grp) * pp.row_bytes;
+      const float rstd = rstd_in;
+      // pass 1: dot = sum(dn*w*xhat), dweight terms dn*xhat
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int c = (j * TPR + lt) * VEC;
+        if (valid && c < N) {
+          float w[VEC], xf[VEC], dn[VEC];
+          unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
+          unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
+          if constexpr (ROPE) rope_pipe_bwd<T, VEC>(dn, c, dyp, a, row);
+          row_weight<VEC>(ws, a, c, wv, w);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) {
+            const float xh = xf[e] * rstd;
+            if (e & 1) d1 = fmaf(dn[e] * w[e], xh, d1);
+            else d0 = fmaf(dn[e] * w[e], xh, d0);
+            acc_fma(acc[j][e], dn[e], xh);
+          }
+        }
+      }
+      const float dot = RR::sum(d0 + d1, red, grp, lt, parity) * inv_n;
+      // pass 2: dx = rstd*(dn*w - xhat*dot), dn and xhat re-read from the slot
+      if (valid) {
+        T* dxr = reinterpret_cast<T*>(a.out) + row * a.ldo;
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          const int c = (j * TPR + lt) * VEC;
+          if (c < N) {
+            float w[VEC], xf[VEC], dn[VEC], o[VEC];
+            unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
+            unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
+            if constexpr (ROPE) rope_pipe_bwd<T, VEC>(dn, c, dyp, a, row);
+            row_weight<VEC>(ws, a, c, wv, w);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) o[e] = rstd * fmaf(-(xf[e] * rstd), dot, dn[e] * w[e]);
+            stg_pack<T, VEC>(dxr + c, pack<T, VEC>(o));
+          }
+        }
+      }
+    }
+    // release the slot: order this thread's reads before the next bulk write
+    fence_proxy_async_smem();
+    __syncthreads();
+  }
+
+  if constexpr (BWD) {
+    // Fold the RPC row groups' accumulators into group 0 in a fixed order
+    // through the idle ring memory, then write this CTA's partial row.
+    __syncthreads();
+    if constexpr (RPC > 1) {
+      AccT* buf = reinterpret_cast<AccT*>(smem);
+      for (int g = RPC - 1; g >= 1; --g) {
+        if (grp == g) {
+#pragma unroll
+          for (int j = 0; j < VPT; ++j)
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) buf[(j * TPR + lt) * VEC + e] = acc[j][e];
+        }
+        __syncthreads();
+        if (grp == 0) {
+#pragma unroll
+          for (int j = 0; j < VPT; ++j)
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) acc[j][e] += buf[(j * TPR + lt) * VEC + e];
+        }
+        __syncthreads();
+      }
+    }
+    if (grp == 0) {
+      AccT* part = reinterpret_cast<AccT*>(a.partials) + (int64_t)blockIdx.x * N;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int c = (j * TPR + lt) * VEC;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e)
+          if (c + e < N) part[c + e] = acc[j][e];
+      }
+    }
+  }
+}
+
+}  // namespace bloth

@@ -58,6 +58,12 @@ const char* bloth_strerror(int status);
    this library (0 if none). */
 int bloth_last_cuda_error(void);
 
+/* Fault bits kernels recorded on the current device since the last reset
+   (bit 0: a bulk-copy completion wait gave up after its time limit and the
+   kernel returned early; its outputs are invalid). Synchronises with the
+   device; reset != 0 clears the bits. Negative on a CUDA error. */
+int bloth_device_fault(int reset);
+
 /* ------------------------------------------------------------------------
  * RMSNorm over rows of N: y = x * rsqrt(mean(x^2) + eps) * w, computed in
  * fp32 and rounded once to the type of x; rstd[M] (fp32) saved for backward.

@@ -22,4 +22,9 @@ from .reference_path import (  # noqa: F401
     rope,
     rope_fwd_bwd,
     packed_position_ids,
+    rms_norm_dw_scale,
+    rms_norm_dx_scale,
+    qk_dw_scale,
+    qk_dx_scale,
+    tolerance_ok,
 )

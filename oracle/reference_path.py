@@ -280,6 +280,36 @@ def qk_dw_scale(x, dy, position_ids=None, inv_f=None, eps: float = 1e-6, cos=Non
     return torch.sqrt((t * t).reshape(-1, D).sum(0))
 
 
+def rms_norm_dx_scale(x, w, dy, eps: float = 1e-6, compute=F64, dy_mag=None):
+    """Elementwise operand magnitude of dx = rstd * (dy*w - xhat*dot):
+    rstd * (|dy|*|w| + |xhat*dot|). An fp32 evaluation of the difference
+    carries an error proportional to this, which rows of zeros
+    (rstd = 1/sqrt(eps)) amplify far beyond |dx|. ``dy_mag`` replaces |dy|
+    when dy is itself a sum (the rotated gradient of the fused op)."""
+    xc, wc = x.to(compute), w.to(compute)
+    g = dy.to(compute) * wc
+    rstd = 1.0 / torch.sqrt((xc * xc).mean(-1, keepdim=True) + eps)
+    xh = xc * rstd
+    dot = (g * xh).mean(-1, keepdim=True)
+    mag = dy.to(compute).abs() if dy_mag is None else dy_mag
+    return rstd * (mag * wc.abs() + (xh * dot).abs())
+
+
+def qk_dx_scale(x, w, dy, position_ids=None, inv_f=None, eps: float = 1e-6, cos=None,
+                sin=None, compute=F64):
+    """:func:`rms_norm_dx_scale` for a head tensor: dy is rotated back
+    (dn = R^T dy), and |dn| is replaced by the magnitude of its two terms."""
+    B, S, _, D = x.shape
+    pos = _positions(B, S, position_ids, x.device)
+    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
+    g = dy.to(compute)
+    h = D // 2
+    g1, g2 = g[..., :h], g[..., h:]
+    dn = torch.cat([g1 * c + g2 * s, g2 * c - g1 * s], -1)
+    mag = torch.cat([(g1 * c).abs() + (g2 * s).abs(), (g2 * c).abs() + (g1 * s).abs()], -1)
+    return rms_norm_dx_scale(x, w, dn, eps, compute, dy_mag=mag)
+
+
 def tolerance_ok(got: torch.Tensor, ref: torch.Tensor, dtype: torch.dtype,
                  scale_with_magnitude: bool = False, scale: torch.Tensor | None = None
                  ) -> tuple[bool, float]:
