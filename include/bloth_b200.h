@@ -90,6 +90,25 @@ int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, 
                       int dtype, int w_dtype, void* workspace, size_t workspace_bytes,
                       void* stream);
 
+/* Bytes of the static device scratch that bloth_rmsnorm_bwd_noalloc uses in
+   place of a workspace (held by every GPU that loads the library). */
+#define BLOTH_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+/* bloth_rmsnorm_bwd for callers that cannot allocate device memory (an
+   operator interface that passes only inputs and outputs, or a process whose
+   device memory is reserved by another allocator). Same arguments minus the
+   workspace, same results: the weight-gradient partial sums live in a
+   library-owned static device array of BLOTH_NOALLOC_SCRATCH_BYTES. Returns
+   BLOTH_ERR_WORKSPACE, doing nothing, when the call needs more partial-sum
+   space than that (bloth_rmsnorm_bwd_workspace_bytes(M, N, dtype) >
+   BLOTH_NOALLOC_SCRATCH_BYTES). Allocates nothing. The first call on each
+   device sets up the array's device address (make it before any stream
+   capture). All calls share the array, so calls that overlap on the GPU race.
+   No counterpart in the reference. */
+int bloth_rmsnorm_bwd_noalloc(const void* dy, int64_t lddy, const void* x, int64_t ldx,
+                              const void* w, const float* rstd, void* dx, int64_t lddx, void* dw,
+                              int64_t M, int64_t N, int dtype, int w_dtype, void* stream);
+
 /* ------------------------------------------------------------------------
  * Fused RMSNorm + rotate-half RoPE with per-row cos/sin tables, the
  * reference's fused_norm_rope(x, weight, cos, sin, eps) contract: each row of
