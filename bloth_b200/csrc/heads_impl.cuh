@@ -6,15 +6,15 @@
 // cos/sin once - either evaluated in-register from the position and
 // inv_freq, each lane computing D/64 of the D/2 angles and the lanes
 // exchanging them by shuffle, or read from a table row - and reuses them for
-// every q and k head of that token. A head row of D elements is held by LPR
-// lanes, one or two 16-byte vectors per lane, so a warp covers RPW = 32/LPR
-// rows per step. The kernels themselves (bulk-copy pipeline) are in
-// heads_pipe.cuh.
+// every q and k head of that token. A head row of D elements is held by
+// LPR = D / (2 * VEC) lanes (8 at D = 128 bf16), each with two 16-byte
+// vectors: columns li*VEC.. of the first half and D/2 + li*VEC.. of the
+// second. A warp covers RPW = 32/LPR rows per step. The kernels themselves
+// (bulk-copy pipeline) are in heads_pipe.cuh.
 //
-// Pairing. Column c pairs with c + D/2. With one vector per lane the partner
-// vector sits in lane li ^ (LPR/2) of the same row group and is fetched with
-// __shfl_xor_sync; with two vectors per lane (D*sizeof(T) = 1 KiB) the partner
-// is the lane's other vector.
+// Pairing. Column c pairs with c + D/2, which is always the lane's other
+// vector: the rotation needs no data exchange between lanes, and a row's sum
+// is a log2(LPR)-level butterfly.
 //
 // Math (fp32 throughout, one rounding on store), following the reference's
 // fused kernel (bloth/bloth/kernels/fused_norm_qkv_rope.py:59-92) per row:
@@ -65,47 +65,36 @@ template <typename T, int D>
 struct HG {
   static constexpr int VEC = 16 / sizeof(T);
   static constexpr int NV = D / VEC;               // vectors per row
-  static constexpr int LPR = NV < 32 ? NV : 32;     // lanes per row
-  static constexpr int VPL = NV / LPR;              // vectors per lane
-  static constexpr int RPW = 32 / LPR;              // rows per warp step
+  static constexpr int LPR = NV / 2;               // lanes per row
+  static constexpr int VPL = 2;                    // vectors per lane: one in each half
+  static constexpr int RPW = 32 / LPR;             // rows per warp step
   static constexpr int HALF = D / 2;
-  static constexpr int APL = HALF / 32;             // angles evaluated per lane
+  static constexpr int APL = HALF / 32;            // angles evaluated per lane
   static_assert(D % (2 * VEC) == 0, "head_dim must be a multiple of 2 vectors");
-  static_assert(VPL == 1 || VPL == 2, "one or two vectors per lane");
+  static_assert(LPR >= 1 && LPR <= 32 && (LPR & (LPR - 1)) == 0, "lanes per row: power of 2");
   static_assert(APL >= 1 && VEC % APL == 0, "angle split must divide the vector");
 };
 
+// Slot 0 of every lane lies in the first half of the row, slot 1 in the second.
 template <typename T, int D>
 __device__ __forceinline__ bool slot_first(int j, int li) {
-  using G = HG<T, D>;
-  if constexpr (G::VPL == 1) return li < G::LPR / 2;
-  else return j == 0;
+  (void)li;
+  return j == 0;
 }
 
-// Column of element e of slot j in lane li.
+// Column of element 0 of slot j in lane li.
 template <typename T, int D>
 __device__ __forceinline__ int slot_col(int j, int li) {
   using G = HG<T, D>;
   return (j * G::LPR + li) * G::VEC;
 }
 
-// Partner vector of slot j: the row's other half.
+// Partner values of both slots: each slot's partner is the lane's other slot.
 template <typename T, int D>
 __device__ __forceinline__ void partner(const Pack<T, HG<T, D>::VEC> (&v)[HG<T, D>::VPL],
                                         float (&pf)[HG<T, D>::VPL][HG<T, D>::VEC]) {
-  using G = HG<T, D>;
-  if constexpr (G::VPL == 1) {
-    uint32_t wds[4];
-    memcpy(wds, &v[0], 16);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) wds[q] = __shfl_xor_sync(0xffffffffu, wds[q], G::LPR / 2);
-    Pack<T, G::VEC> pk;
-    memcpy(&pk, wds, 16);
-    unpack(pk, pf[0]);
-  } else {
-    unpack(v[1], pf[0]);
-    unpack(v[0], pf[1]);
-  }
+  unpack(v[1], pf[0]);
+  unpack(v[0], pf[1]);
 }
 
 template <typename T, int D>

@@ -8,8 +8,9 @@
 // then C1 chunks of k. Warp gw owns tokens gw, gw + W, gw + 2W, ... (W = warps
 // in the grid) and walks their chunks in order; before computing chunk g it
 // issues the copy of chunk g + NST - 1 into the slot that chunk g - 1 has just
-// released, so NST - 1 chunks (8 KiB per warp, 128 KiB per SM of 16 warps)
-// are in flight while one is computed. Lane 0 issues one bulk copy per chunk and
+// released, so NST - 1 chunks (8-12 KiB per warp, 128-150 KiB per SM) are in
+// flight while one is computed. The backward runs 12 warps per CTA (more
+// registers per lane for its gradient state), the forward 16. Lane 0 issues one bulk copy per chunk and
 // tensor when the token's heads are contiguous (head stride == D), else lanes
 // issue one copy per row. The backward chunk carries the output gradient
 // rows, the forward input rows and (when 16-byte aligned) the rows' rstd.
@@ -37,10 +38,12 @@ struct HP {
   static constexpr int RSTD_OFF = NT * R * ROWB;
   static constexpr bool RSTD_BULK = BWD && (R % 4 == 0);     // rstd rows fill 16-byte units
   static constexpr int SLOT = RSTD_OFF + (BWD ? ((R * 4 + 15) / 16) * 16 : 0);
-  static constexpr int NST = 3;                              // ring slots per warp
-  static constexpr int WPB = 16;                             // warps per CTA
+  static constexpr int NST = BWD ? 4 : 3;                    // ring slots per warp
+  static constexpr int WPB = BWD ? 12 : 16;                  // warps per CTA
   static constexpr int RING = WPB * NST * SLOT;
-  static constexpr int SMEM = RING + WPB * NST * 8;          // + one mbarrier per slot
+  static constexpr int BARS = RING;                          // one mbarrier per slot
+  static constexpr int WSM = BARS + WPB * NST * 8;           // q and k weights, fp32 [2][D]
+  static constexpr int SMEM = WSM + 2 * D * 4;
   static_assert(R % G::RPW == 0, "chunk rows must fill whole warp steps");
   static_assert(SLOT % 16 == 0, "bulk-copy destinations must be 16-byte aligned");
   static_assert(SMEM <= 227 * 1024, "ring must fit in shared memory");
@@ -56,23 +59,43 @@ struct FwdCoef {
   float be[HG<T, D>::VPL][HG<T, D>::VEC];
 };
 
+// Coefficients for the lane's two slots from its own-column weights w (slot
+// j's partner column is slot 1-j's column, so its weight is w[1-j]).
 template <typename T, int D>
 __device__ __forceinline__ void make_fwd_coef(FwdCoef<T, D>& k,
-                                              const float (&wo)[HG<T, D>::VPL][HG<T, D>::VEC],
-                                              const float (&wp)[HG<T, D>::VPL][HG<T, D>::VEC],
+                                              const float (&w)[HG<T, D>::VPL][HG<T, D>::VEC],
                                               const float (&cs)[HG<T, D>::VEC],
-                                              const float (&sn)[HG<T, D>::VEC], int li) {
+                                              const float (&sn)[HG<T, D>::VEC]) {
   using G = HG<T, D>;
 #pragma unroll
-  for (int j = 0; j < G::VPL; ++j) {
-    const bool first = slot_first<T, D>(j, li);
-#pragma unroll
-    for (int e = 0; e < G::VEC; ++e) {
-      k.al[j][e] = wo[j][e] * cs[e];
-      const float b = wp[j][e] * sn[e];
-      k.be[j][e] = first ? -b : b;
-    }
+  for (int e = 0; e < G::VEC; ++e) {
+    k.al[0][e] = w[0][e] * cs[e];
+    k.al[1][e] = w[1][e] * cs[e];
+    k.be[0][e] = -(w[1][e] * sn[e]);  // first half:  y1 = n1*cos - n2*sin
+    k.be[1][e] = w[0][e] * sn[e];     // second half: y2 = n1*sin + n2*cos
   }
+}
+
+// The lane's own-column weights of tensor `ten` from the fp32 copy in shared
+// memory (all ones for RoPE alone).
+template <typename T, int D, bool NORM>
+__device__ __forceinline__ void lane_weights(const float* wsm, int ten, int li,
+                                             float (&w)[HG<T, D>::VPL][HG<T, D>::VEC]) {
+  using G = HG<T, D>;
+#pragma unroll
+  for (int j = 0; j < G::VPL; ++j)
+#pragma unroll
+    for (int e = 0; e < G::VEC; e += 4) {
+      if constexpr (NORM) {
+        const float4 v = *reinterpret_cast<const float4*>(wsm + ten * D + slot_col<T, D>(j, li) + e);
+        w[j][e] = v.x;
+        w[j][e + 1] = v.y;
+        w[j][e + 2] = v.z;
+        w[j][e + 3] = v.w;
+      } else {
+        w[j][e] = w[j][e + 1] = w[j][e + 2] = w[j][e + 3] = 1.f;
+      }
+    }
 }
 
 // One chunk of the forward: rows r0 .. r0+rc-1 of tensor TEN of token (b, s).
@@ -134,14 +157,14 @@ __device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned
   }
 }
 
-// One chunk of the backward: dn = R^T dy = dy_own*cos + dy_partner*sn_signed
-// (sn_signed = +sin in the first half, -sin in the second), g = dn*w,
-// dx = rstd*(g - xhat*sum(g*xhat)/D), dweight += dn*xhat.
+// One chunk of the backward: dn = R^T dy = dy_own*cos + dy_partner*sin in
+// the first half (slot 0), dy_own*cos - dy_partner*sin in the second
+// (slot 1); g = dn*w, dx = rstd*(g - xhat*sum(g*xhat)/D), dweight += dn*xhat.
 template <typename T, int D, int TEN>
 __device__ __forceinline__ void pipe_bwd_chunk(
     const HeadArgs& a, const unsigned char* slot, int64_t t, int64_t b, int64_t s, int r0,
     int rc, const float (&wo)[HG<T, D>::VPL][HG<T, D>::VEC], const float (&cs)[HG<T, D>::VEC],
-    const float (&sp)[HG<T, D>::VPL][HG<T, D>::VEC],
+    const float (&sn)[HG<T, D>::VEC],
     typename AccOf<T>::type (&acc)[HG<T, D>::VPL][HG<T, D>::VEC], int rg, int li) {
   using G = HG<T, D>;
   using P = HP<T, D, kHeadNormBwd>;
@@ -181,7 +204,7 @@ __device__ __forceinline__ void pipe_bwd_chunk(
       unpack(xp[j], xf);
 #pragma unroll
       for (int e = 0; e < G::VEC; ++e) {
-        const float dn = fmaf(pf[j][e], sp[j][e], gf[j][e] * cs[e]);
+        const float dn = fmaf(j == 0 ? pf[j][e] : -pf[j][e], sn[e], gf[j][e] * cs[e]);
         xh[j][e] = xf[e] * rstd;
         g[j][e] = dn * wo[j][e];
         if (e & 1) d1 = fmaf(g[j][e], xh[j][e], d1);
@@ -238,9 +261,9 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   const int warp = threadIdx.x >> 5;
   const int rg = lane / G::LPR;
   const int li = lane % G::LPR;
-  const int pg = G::VPL == 1 ? li % (G::LPR / 2) : li;
+  const int pg = li;  // the lane's pair indices are li*VEC .. li*VEC+VEC-1
   unsigned char* ring = smem + warp * P::NST * P::SLOT;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::RING) + warp * P::NST;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + P::BARS) + warp * P::NST;
   if (lane == 0) {
 #pragma unroll
     for (int q = 0; q < P::NST; ++q) mbar_init(&bars[q], 1);
@@ -253,27 +276,15 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   for (int q = 0; q < G::APL; ++q)
     invf[q] = a.inv_freq ? __ldg(a.inv_freq + lane * G::APL + q) : 0.f;
 
-  // Weights of the lane's columns (and, forward, of their partner columns).
-  float wo[2][G::VPL][G::VEC], wp[2][G::VPL][G::VEC];
-#pragma unroll
-  for (int q = 0; q < 2; ++q)
-#pragma unroll
-    for (int j = 0; j < G::VPL; ++j) {
-      if (NORM && a.H[q] != 0) {
-        const int c = slot_col<T, D>(j, li);
-        ld_any_vec<G::VEC>(a.w[q], c, a.w_dt, true, wo[q][j]);
-        if constexpr (!BWD) {
-          const int pc = c < G::HALF ? c + G::HALF : c - G::HALF;
-          ld_any_vec<G::VEC>(a.w[q], pc, a.w_dt, true, wp[q][j]);
-        }
-      } else {
-#pragma unroll
-        for (int e = 0; e < G::VEC; ++e) wo[q][j][e] = 1.f;
-      }
-      if (BWD || !NORM || a.H[q] == 0)
-#pragma unroll
-        for (int e = 0; e < G::VEC; ++e) wp[q][j][e] = 1.f;
+  // Weights of q and k as fp32 in shared memory, shared by the CTA's warps.
+  float* wsm = reinterpret_cast<float*>(smem + P::WSM);
+  if constexpr (NORM) {
+    for (int c = threadIdx.x; c < 2 * D; c += P::WPB * 32) {
+      const int q = c / D;
+      wsm[c] = a.H[q] != 0 ? ld_any(a.w[q], c - q * D, a.w_dt) : 0.f;
     }
+  }
+  __syncthreads();
   AccT acc[2][G::VPL][G::VEC];
 #pragma unroll
   for (int q = 0; q < 2; ++q)
@@ -333,8 +344,8 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   }
 
   float cs[G::VEC], sn[G::VEC];
-  FwdCoef<T, D> kq, kk;            // forward coefficients of q and k for the current token
-  float sp[G::VPL][G::VEC];        // backward: signed sin per slot
+  FwdCoef<T, D> kc;                // forward: coefficients of the current tensor and token
+  float wc[G::VPL][G::VEC];        // backward: weights of the current tensor
   int64_t pos_next = my_tok > 0 ? token_pos<T, D>(a, cc.b, cc.s) : 0;
   const float sgn = a.transpose ? -1.f : 1.f;
   int csl = 0;
@@ -361,19 +372,17 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
 #pragma unroll
         for (int e = 0; e < G::VEC; ++e) sn[e] *= sgn;
       }
-      if constexpr (BWD) {
-#pragma unroll
-        for (int jj = 0; jj < G::VPL; ++jj) {
-          const bool first = slot_first<T, D>(jj, li);
-#pragma unroll
-          for (int e = 0; e < G::VEC; ++e) sp[jj][e] = first ? sn[e] : -sn[e];
-        }
-      } else {
-        make_fwd_coef<T, D>(kq, wo[0], wp[0], cs, sn, li);
-        if (C1 > 0) make_fwd_coef<T, D>(kk, wo[1], wp[1], cs, sn, li);
-      }
     }
     const int ten = cc.j < C0 ? 0 : 1;
+    if (cc.j == 0 || cc.j == C0) {  // new token or switch from q to k: this tensor's weights
+      if constexpr (BWD) {
+        lane_weights<T, D, NORM>(wsm, ten, li, wc);
+      } else {
+        float w[G::VPL][G::VEC];
+        lane_weights<T, D, NORM>(wsm, ten, li, w);
+        make_fwd_coef<T, D>(kc, w, cs, sn);
+      }
+    }
     const int r0 = (ten == 0 ? cc.j : cc.j - C0) * P::R;
     const int rc = min(P::R, a.H[ten] - r0);
     const bool landed = mbar_wait(&bars[csl], cph, a.fault);
@@ -381,12 +390,12 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
     const unsigned char* slot = ring + csl * P::SLOT;
     if constexpr (BWD) {
       if (ten == 0)
-        pipe_bwd_chunk<T, D, 0>(a, slot, cc.t, cc.b, cc.s, r0, rc, wo[0], cs, sp, acc[0], rg, li);
+        pipe_bwd_chunk<T, D, 0>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[0], rg, li);
       else
-        pipe_bwd_chunk<T, D, 1>(a, slot, cc.t, cc.b, cc.s, r0, rc, wo[1], cs, sp, acc[1], rg, li);
+        pipe_bwd_chunk<T, D, 1>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[1], rg, li);
     } else {
-      if (ten == 0) pipe_fwd_chunk<T, D, MODE, 0>(a, slot, cc.t, cc.b, cc.s, r0, rc, kq, rg, li);
-      else pipe_fwd_chunk<T, D, MODE, 1>(a, slot, cc.t, cc.b, cc.s, r0, rc, kk, rg, li);
+      if (ten == 0) pipe_fwd_chunk<T, D, MODE, 0>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
+      else pipe_fwd_chunk<T, D, MODE, 1>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
     }
     // release the slot: order this lane's reads before the next bulk write
     fence_proxy_async_smem();
