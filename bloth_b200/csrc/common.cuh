@@ -75,8 +75,20 @@ __device__ __forceinline__ void stg_pack(T* p, const Pack<T, VEC>& v) {
 
 template <typename T, int VEC>
 __device__ __forceinline__ void unpack(const Pack<T, VEC>& pk, float (&f)[VEC]) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC % 2 == 0) {
+    // A bf16 value is the upper half of the fp32 with the same bits, so each
+    // element of a packed pair converts with one shift or mask of the word.
+    uint32_t w[VEC / 2];
+    memcpy(w, &pk, sizeof(w));
 #pragma unroll
-  for (int e = 0; e < VEC; ++e) f[e] = to_f(pk.v[e]);
+    for (int q = 0; q < VEC / 2; ++q) {
+      f[2 * q] = __uint_as_float(w[q] << 16);
+      f[2 * q + 1] = __uint_as_float(w[q] & 0xffff0000u);
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) f[e] = to_f(pk.v[e]);
+  }
 }
 
 // Rounds VEC floats to T (nearest even); 16-bit types convert two at a time

@@ -197,7 +197,7 @@ __device__ __forceinline__ void pipe_bwd_chunk(
     for (int j = 0; j < G::VPL; ++j) unpack(gp[j], gf[j]);
     partner<T, D>(gp, pf);
     float g[G::VPL][G::VEC], xh[G::VPL][G::VEC];
-    float d0 = 0.f, d1 = 0.f;
+    float dd[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < G::VPL; ++j) {
       float xf[G::VEC];
@@ -207,12 +207,11 @@ __device__ __forceinline__ void pipe_bwd_chunk(
         const float dn = fmaf(j == 0 ? pf[j][e] : -pf[j][e], sn[e], gf[j][e] * cs[e]);
         xh[j][e] = xf[e] * rstd;
         g[j][e] = dn * wo[j][e];
-        if (e & 1) d1 = fmaf(g[j][e], xh[j][e], d1);
-        else d0 = fmaf(g[j][e], xh[j][e], d0);
+        dd[e & 3] = fmaf(g[j][e], xh[j][e], dd[e & 3]);
         if (valid) acc_add(acc[j][e], dn, xh[j][e]);
       }
     }
-    const float dot = group_lane_sum<G::LPR>(d0 + d1) * kInvD;
+    const float dot = group_lane_sum<G::LPR>((dd[0] + dd[1]) + (dd[2] + dd[3])) * kInvD;
     if (valid) {
       T* drow = dptr + (int64_t)(u * G::RPW) * dsh;
 #pragma unroll

@@ -40,11 +40,10 @@ int launch_row_bwd(const RowArgs& a0, void* ws, size_t ws_bytes, void* dw, cudaS
                                 a0.w_dt, st);
 }
 
-// Shared-memory plan of the pipelined row kernels for rows of N: ring slots,
-// whether the fp32 weight copy is staged, within a per-CTA budget that leaves
-// room for several CTAs per SM (72 KB for 128-thread CTAs, 112 KB for 256,
-// 200 KB for larger). nst == 0 when even two slots do not fit (the register
-// kernels then take the rows).
+// Shared-memory plan of the pipelined row kernels for rows of N: ring slots
+// within a per-CTA budget that leaves room for several CTAs per SM (72 KB for
+// 128-thread CTAs, 112 KB for 256, 200 KB for larger); nst == 0 when even
+// two slots do not fit (the register kernels then take the rows).
 template <typename T, typename PC, bool BWD>
 RowPipe pipe_plan(int N, bool contiguous) {
   RowPipe pp;
@@ -53,17 +52,15 @@ RowPipe pipe_plan(int N, bool contiguous) {
   pp.contiguous = contiguous ? 1 : 0;
   pp.fault = fault_word();
   const size_t budget = PC::BLOCK <= 128 ? 72 * 1024 : (PC::BLOCK <= 256 ? 112 * 1024 : 200 * 1024);
-  const size_t slot = (size_t)pp.slot_bytes + 8;
-  const size_t wbytes = (size_t)N * 4;
-  pp.w_staged = wbytes <= 32 * 1024 && budget >= wbytes + 2 * slot ? 1 : 0;
-  const size_t avail = budget - (pp.w_staged ? wbytes : 0);
-  const size_t n = avail / slot;
+  const size_t n = budget / ((size_t)pp.slot_bytes + 8);
   pp.nst = n >= 4 ? 4 : (n >= 2 ? (int)n : 0);
+  (void)N;
   return pp;
 }
 
 inline size_t pipe_smem(const RowPipe& pp, int N) {
-  return (size_t)pp.nst * (pp.slot_bytes + 8) + (pp.w_staged ? (size_t)N * 4 : 0);
+  (void)N;
+  return (size_t)pp.nst * (pp.slot_bytes + 8);
 }
 
 // Grid of the pipelined kernel (one wave of resident CTAs or fewer), or -1 if

@@ -27,7 +27,6 @@ struct RowPipe {
   int row_bytes;     // N * sizeof(T), a multiple of 16
   int slot_bytes;    // RPC * row_bytes * (1 forward, 2 backward)
   int contiguous;    // rows of a block are adjacent in memory (ld == N) for every input
-  int w_staged;      // the weight is converted to fp32 into shared memory once per CTA
   unsigned int* fault;
 };
 
@@ -43,25 +42,6 @@ struct PipeCfg {
   static constexpr int BLOCK = TPR * RPC;
   static constexpr int MIN_BLOCKS = BLOCK >= 512 ? 1 : 512 / BLOCK;
 };
-
-// Weight values for columns c..c+VEC-1: from the fp32 copy in shared memory
-// when staged, else from global memory.
-template <int VEC>
-__device__ __forceinline__ void row_weight(const float* ws, const RowArgs& a, int c, bool wv,
-                                           float (&w)[VEC]) {
-  if (ws != nullptr) {
-#pragma unroll
-    for (int q = 0; q < VEC; q += 4) {
-      const float4 v = *reinterpret_cast<const float4*>(ws + c + q);
-      w[q] = v.x;
-      w[q + 1] = v.y;
-      w[q + 2] = v.z;
-      w[q + 3] = v.w;
-    }
-  } else {
-    ld_any_vec<VEC>(a.w, c, a.w_dt, wv, w);
-  }
-}
 
 template <typename T, int VEC>
 __device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsigned char* rowp,
@@ -135,7 +115,7 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
 }
 
 template <typename T, int VEC, int TPR, int VPT, int RPC, bool ROPE, bool BWD>
-__global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 512 ? 1 : 512 / (TPR * RPC))
+__global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * RPC))
     row_pipe_kernel(const RowArgs a, const RowPipe pp) {
   using RR = RowReduce<TPR, RPC>;
   using AccT = typename AccOf<T>::type;
@@ -147,15 +127,24 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 512 ? 1 : 512 / (TPR * 
   const float inv_n = 1.0f / (float)N;
   const bool wv = a.w_vec != 0;
   const int NST = pp.nst;
-  float* ws = pp.w_staged ? reinterpret_cast<float*>(smem + (size_t)NST * pp.slot_bytes) : nullptr;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * pp.slot_bytes +
-                                               (pp.w_staged ? (size_t)N * 4 : 0));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * pp.slot_bytes);
   if (threadIdx.x == 0) {
     for (int q = 0; q < NST; ++q) mbar_init(&bars[q], 1);
     mbar_init_fence();
   }
-  if (ws != nullptr)
-    for (int c = threadIdx.x; c < N; c += TPR * RPC) ws[c] = ld_any(a.w, c, a.w_dt);
+  // The thread's columns are the same for every row it processes: keep their
+  // weights in registers (VPT * VEC <= 32 for every pipelined shape).
+  float wr[VPT][VEC];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = (j * TPR + lt) * VEC;
+    if (c < N) {
+      ld_any_vec<VEC>(a.w, c, a.w_dt, wv, wr[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) wr[j][e] = 0.f;
+    }
+  }
   __syncthreads();
 
   const int64_t nblk = (a.M + RPC - 1) / RPC;
@@ -253,11 +242,10 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 512 ? 1 : 512 / (TPR * 
         for (int j = 0; j < VPT; ++j) {
           const int c = (j * TPR + lt) * VEC;
           if (c < N) {
-            float f[VEC], w[VEC];
+            float f[VEC];
             unpack(xp[j], f);
-            row_weight<VEC>(ws, a, c, wv, w);
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) f[e] = f[e] * rstd * w[e];
+            for (int e = 0; e < VEC; ++e) f[e] = f[e] * rstd * wr[j][e];
             if constexpr (ROPE) rope_pipe_fwd<T, VEC>(f, c, rowp, rstd, a, row);
             stg_pack<T, VEC>(yr + c, pack<T, VEC>(f));
           }
@@ -273,16 +261,15 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 512 ? 1 : 512 / (TPR * 
       for (int j = 0; j < VPT; ++j) {
         const int c = (j * TPR + lt) * VEC;
         if (valid && c < N) {
-          float w[VEC], xf[VEC], dn[VEC];
+          float xf[VEC], dn[VEC];
           unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
           unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
           if constexpr (ROPE) rope_pipe_bwd<T, VEC>(dn, c, dyp, a, row);
-          row_weight<VEC>(ws, a, c, wv, w);
 #pragma unroll
           for (int e = 0; e < VEC; ++e) {
             const float xh = xf[e] * rstd;
-            if (e & 1) d1 = fmaf(dn[e] * w[e], xh, d1);
-            else d0 = fmaf(dn[e] * w[e], xh, d0);
+            if (e & 1) d1 = fmaf(dn[e] * wr[j][e], xh, d1);
+            else d0 = fmaf(dn[e] * wr[j][e], xh, d0);
             acc_fma(acc[j][e], dn[e], xh);
           }
         }
@@ -295,13 +282,12 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 512 ? 1 : 512 / (TPR * 
         for (int j = 0; j < VPT; ++j) {
           const int c = (j * TPR + lt) * VEC;
           if (c < N) {
-            float w[VEC], xf[VEC], dn[VEC], o[VEC];
+            float xf[VEC], dn[VEC], o[VEC];
             unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
             unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
             if constexpr (ROPE) rope_pipe_bwd<T, VEC>(dn, c, dyp, a, row);
-            row_weight<VEC>(ws, a, c, wv, w);
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) o[e] = rstd * fmaf(-(xf[e] * rstd), dot, dn[e] * w[e]);
+            for (int e = 0; e < VEC; ++e) o[e] = rstd * fmaf(-(xf[e] * rstd), dot, dn[e] * wr[j][e]);
             stg_pack<T, VEC>(dxr + c, pack<T, VEC>(o));
           }
         }
