@@ -74,6 +74,28 @@ def step_bytes(tokens: int, name: str, elem: int = 2) -> dict:
     return out
 
 
+# ------------------------------------------------------------- ranks
+def local_batch(batch: int, world: int, scaling: str) -> int:
+    """Batch rows (sequences) one rank processes: the full batch per rank
+    under weak scaling, an equal share of it under strong scaling."""
+    if scaling == "weak":
+        return batch
+    if batch % world:
+        raise ValueError(f"strong scaling needs batch {batch} divisible by {world} ranks")
+    return batch // world
+
+
+def max_over_ranks(value: float, dist, device) -> float:
+    """Largest `value` over all ranks (the job finishes with its slowest rank);
+    `value` itself when not distributed."""
+    if dist is None:
+        return value
+    import torch as _t
+    t = _t.tensor([value], device=device, dtype=_t.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 # ------------------------------------------------------------- inputs
 def make_inputs(name: str, tokens_b: int, dev, seed: int, shard=(0, 1)):
     """Seeded synthetic inputs on `dev` for batch rows shard[0]::shard[1]."""
@@ -310,12 +332,7 @@ def main() -> None:
                                 device_id=dev)
 
     # tokens this rank processes per step
-    if args.scaling == "weak":
-        b_local = B
-    else:
-        if B % world:
-            raise SystemExit(f"strong scaling needs batch {B} divisible by {world}")
-        b_local = B // world
+    b_local = local_batch(B, world, args.scaling)
     tokens_local = b_local * S
     inp = make_inputs(name, b_local, dev, seed=1234 + rank, shard=(rank, world))
     nbytes = step_bytes(tokens_local, name)
@@ -325,32 +342,60 @@ def main() -> None:
             dist.barrier()
         torch.cuda.synchronize()
 
-    for _ in range(args.warmup):
-        run_step(inp, bloth)
+    # ---- one fwd+bwd step through the public API, captured as a CUDA graph
+    # (UNROLL steps per graph) with an event pair around every C-ABI launch;
+    # replaying it runs every kernel of every step without host gaps.
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(max(args.warmup, 3)):
+            run_step(inp, bloth)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    unroll = next(u for u in (10, 8, 5, 4, 2, 1) if args.steps % u == 0)  # exactly K steps
+    graph = torch.cuda.CUDAGraph()
+    with _lib.timing_launches(external=True) as timer:
+        with torch.cuda.graph(graph):
+            for _ in range(unroll):
+                run_step(inp, bloth)
+    replays = max(1, args.steps // unroll)
+    steps = replays * unroll
+    for _ in range(max(1, args.warmup // unroll)):
+        graph.replay()
     barrier()
 
-    # ---- device-resident timed region, per-launch events for the roofline
+    # ---- device-resident timed region
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk, _lib.timing_launches() as timer:
+    with ClockSampler(local) as clk:
         barrier()
         start.record()
-        for _ in range(args.steps):
-            run_step(inp, bloth)
+        for _ in range(replays):
+            graph.replay()
         end.record()
         barrier()
-    ms = start.elapsed_time(end)
-    per_kernel = timer.summary()
-    if dist is not None:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    ms_step = ms / args.steps
+    ms = max_over_ranks(start.elapsed_time(end), dist, dev)
+    per_kernel = timer.summary()  # the last replay's launches
+    ms_step = ms / steps
     tokens_total = tokens_local * world
     value = tokens_total / (ms_step / 1e3)
     gbps = nbytes["total"] * world / (ms_step / 1e3) / 1e9
 
-    # kernels launched per C-ABI call: backward entry points add the dweight reduce
-    launches = sum(v["launches"] * (2 if k.endswith("_bwd") else 1) for k, v in per_kernel.items())
+    # the same step called eagerly from Python (host launch overhead included)
+    eager_steps = min(200, steps)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record()
+    for _ in range(eager_steps):
+        run_step(inp, bloth)
+    e1.record()
+    barrier()
+    eager_ms = max_over_ranks(e0.elapsed_time(e1), dist, dev) / eager_steps
+
+    # kernels launched per C-ABI call (backward entry points add the dweight
+    # reduce); the timer saw one replay of `unroll` steps
+    per_step = sum(v["launches"] * (2 if k.endswith("_bwd") else 1)
+                   for k, v in per_kernel.items()) // unroll
+    launches = per_step * steps
     kb = {"bloth_rmsnorm_fwd": "rms_fwd", "bloth_rmsnorm_bwd": "rms_bwd",
           "bloth_qk_norm_rope_fwd": "qk_fwd", "bloth_qk_norm_rope_bwd": "qk_bwd"}
     top = max(per_kernel.items(), key=lambda kv: kv[1]["total_ms"])
@@ -381,7 +426,7 @@ def main() -> None:
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "steps": steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
             "config": {"workload": describe(name), "tokens_per_gpu": tokens_local,
@@ -391,6 +436,9 @@ def main() -> None:
                        "gbps": round(gbps, 1),
                        "frac_of_8tbs_per_gpu": round(gbps / world / NOMINAL_HBM_GBS, 4),
                        "frac_of_measured_per_gpu": round(gbps / world / peak, 4),
+                       "timing": f"CUDA graph of {unroll} steps through the public API, "
+                                 f"{replays} replays",
+                       "eager_ms_per_step": round(eager_ms, 4),
                        "kernels": kernels},
             "roofline": {"bound": "hbm", "kernel": top[0], "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
@@ -409,39 +457,66 @@ def main() -> None:
 
 
 def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
-    """Same step through the public API with the inputs in pinned host memory:
-    every step copies its inputs host->device and all of its results
-    (outputs and gradients) device->host inside the timed region."""
+    """The same step through the public API with every input in pinned host
+    memory: each step copies its inputs host->device and all of its results
+    (outputs and gradients) device->host inside the timed region. Transfers
+    are pipelined as a streaming user would: step i+1's inputs upload on a
+    copy stream while step i computes, and step i's results download on a
+    third stream (two device input buffers; events order every reuse)."""
     keys_in = [k for k in ("x", "gy", "q", "k", "gq", "gk", "pos") if k in inp]
     host = {k: inp[k].detach().cpu().pin_memory() for k in keys_in}
     small = {k: v for k, v in inp.items() if k not in keys_in}
     h2d = sum(v.numel() * v.element_size() for v in host.values())
+    bufs = [{k: torch.empty_like(inp[k]) for k in keys_in} for _ in range(2)]
+    s_main = torch.cuda.current_stream(dev)
+    s_in = torch.cuda.Stream(dev)
+    s_out = torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in range(2)]
+    ev_free = [torch.cuda.Event() for _ in range(2)]
     outs_host = None
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
-    def one():
+    def upload(i):
+        b = bufs[i % 2]
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(ev_free[i % 2])  # step i-2 has finished reading this buffer
+            for k in keys_in:
+                b[k].copy_(host[k], non_blocking=True)
+            ev_in[i % 2].record(s_in)
+
+    def compute_and_download(i):
         nonlocal outs_host
-        d = {k: v.to(dev, non_blocking=True) for k, v in host.items()}
+        b = bufs[i % 2]
+        s_main.wait_event(ev_in[i % 2])
+        d = {k: b[k].detach() for k in keys_in}
         d.update(small)
         outs, grads = run_step(d, bloth)
+        ev_free[i % 2].record(s_main)
         res = [t.detach() for t in list(outs) + list(grads)]
         if outs_host is None:
             outs_host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in res]
-        for h, t in zip(outs_host, res):
-            h.copy_(t, non_blocking=True)
+        s_out.wait_stream(s_main)
+        with torch.cuda.stream(s_out):
+            for h, t in zip(outs_host, res):
+                t.record_stream(s_out)
+                h.copy_(t, non_blocking=True)
 
-    one()
+    # warm-up pass of the whole pipeline
+    upload(0)
+    compute_and_download(0)
+    torch.cuda.synchronize(dev)
     barrier()
-    start.record()
-    for _ in range(steps):
-        one()
-    end.record()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(s_main)
+    s_in.wait_stream(s_main)
+    upload(0)
+    for i in range(steps):
+        if i + 1 < steps:
+            upload(i + 1)
+        compute_and_download(i)
+    s_main.wait_stream(s_out)
+    end.record(s_main)
     barrier()
-    ms = start.elapsed_time(end)
-    if dist is not None:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = max_over_ranks(start.elapsed_time(end), dist, dev)
     d2h = sum(t.numel() * t.element_size() for t in outs_host)
     return {"value": tokens_total / (ms / steps / 1e3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

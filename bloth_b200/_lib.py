@@ -134,6 +134,21 @@ def stream_of(t: torch.Tensor) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
 
 
+_ws_cache: dict = {}
+
+
+def workspace_bytes(entry: str, device: torch.device, *args) -> int:
+    """Size reported by the C ABI's `entry` (a *_workspace_bytes function) on
+    `device`, cached: it depends only on the sizes and the device."""
+    key = (entry, device.index, args)
+    v = _ws_cache.get(key)
+    if v is None:
+        with torch.cuda.device(device):
+            v = int(getattr(load(), entry)(*args))
+        _ws_cache[key] = v
+    return v
+
+
 def aligned16(t: torch.Tensor) -> torch.Tensor:
     """t itself when its data is 16-byte aligned, else an aligned copy."""
     return t if t.data_ptr() % 16 == 0 else t.clone()
@@ -143,15 +158,23 @@ def aligned16(t: torch.Tensor) -> torch.Tensor:
 class LaunchTimer:
     """Records a CUDA event pair around every C-ABI launch, on the launching
     stream, grouped by entry point. Used by bench.py to time individual
-    kernels inside its timed region."""
+    kernels inside its timed region. With ``external=True`` the events are
+    created so that a CUDA-graph capture turns their records into event-record
+    nodes, which re-record on every replay of the graph."""
 
-    def __init__(self):
+    def __init__(self, external: bool = False):
         self.pairs: dict[str, list] = {}
+        self.external = external
+
+    def _event(self):
+        if self.external:
+            return torch.cuda.Event(enable_timing=True, external=True)
+        return torch.cuda.Event(enable_timing=True)
 
     def wrap(self, name: str, t: torch.Tensor, fn):
         s = torch.cuda.current_stream(t.device)
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
+        a = self._event()
+        b = self._event()
         a.record(s)
         rc = fn()
         b.record(s)
@@ -170,9 +193,9 @@ _timer: LaunchTimer | None = None
 
 
 @contextmanager
-def timing_launches():
+def timing_launches(external: bool = False):
     global _timer
-    prev, _timer = _timer, LaunchTimer()
+    prev, _timer = _timer, LaunchTimer(external)
     try:
         yield _timer
     finally:

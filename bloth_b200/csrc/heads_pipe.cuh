@@ -99,7 +99,8 @@ __device__ __forceinline__ void lane_weights(const float* wsm, int ten, int li,
 }
 
 // One chunk of the forward: rows r0 .. r0+rc-1 of tensor TEN of token (b, s).
-template <typename T, int D, int MODE, int TEN>
+// FULL: rc == R, so every step is unrolled with compile-time offsets.
+template <typename T, int D, int MODE, int TEN, bool FULL>
 __device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned char* slot,
                                                int64_t t, int64_t b, int64_t s, int r0, int rc,
                                                const FwdCoef<T, D>& k, int rg, int li) {
@@ -116,7 +117,7 @@ __device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned
   float* rstd_out = NORM ? a.rstd_out[TEN] + t * a.H[TEN] + r0 + rg : nullptr;
 #pragma unroll
   for (int u = 0; u < P::R / G::RPW; ++u) {
-    if (u * G::RPW >= rc) break;  // partial chunk: no rows left in this step
+    if (!FULL && u * G::RPW >= rc) break;  // partial chunk: no rows left in this step
     const int rl = u * G::RPW + rg;
     Pack<T, G::VEC> xp[G::VPL];
 #pragma unroll
@@ -140,7 +141,7 @@ __device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned
       const float ss = group_lane_sum<G::LPR>(s0 + s1);
       rstd = rsqrtf(fmaf(ss, kInvD, a.eps));
     }
-    if (rl < rc) {
+    if (FULL || rl < rc) {
       T* drow = dptr + (int64_t)(u * G::RPW) * dsh;
 #pragma unroll
       for (int j = 0; j < G::VPL; ++j) {
@@ -160,7 +161,7 @@ __device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned
 // One chunk of the backward: dn = R^T dy = dy_own*cos + dy_partner*sin in
 // the first half (slot 0), dy_own*cos - dy_partner*sin in the second
 // (slot 1); g = dn*w, dx = rstd*(g - xhat*sum(g*xhat)/D), dweight += dn*xhat.
-template <typename T, int D, int TEN>
+template <typename T, int D, int TEN, bool FULL>
 __device__ __forceinline__ void pipe_bwd_chunk(
     const HeadArgs& a, const unsigned char* slot, int64_t t, int64_t b, int64_t s, int r0,
     int rc, const float (&wo)[HG<T, D>::VPL][HG<T, D>::VEC], const float (&cs)[HG<T, D>::VEC],
@@ -180,9 +181,9 @@ __device__ __forceinline__ void pipe_bwd_chunk(
   const bool rstd_in_smem = P::RSTD_BULK && a.rstd_bulk;
 #pragma unroll
   for (int u = 0; u < P::R / G::RPW; ++u) {
-    if (u * G::RPW >= rc) break;  // partial chunk: no rows left in this step
+    if (!FULL && u * G::RPW >= rc) break;  // partial chunk: no rows left in this step
     const int rl = u * G::RPW + rg;
-    const bool valid = rl < rc;
+    const bool valid = FULL || rl < rc;
     const float rstd = rstd_in_smem ? rstd_smem[u * G::RPW]
                                     : (valid ? __ldg(rstd_src + u * G::RPW) : 0.f);
     Pack<T, G::VEC> gp[G::VPL], xp[G::VPL];
@@ -388,13 +389,25 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
     if (!__all_sync(0xffffffffu, landed)) break;
     const unsigned char* slot = ring + csl * P::SLOT;
     if constexpr (BWD) {
-      if (ten == 0)
-        pipe_bwd_chunk<T, D, 0>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[0], rg, li);
-      else
-        pipe_bwd_chunk<T, D, 1>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[1], rg, li);
+      if (ten == 0) {
+        if (rc == P::R)
+          pipe_bwd_chunk<T, D, 0, true>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[0], rg, li);
+        else
+          pipe_bwd_chunk<T, D, 0, false>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[0], rg, li);
+      } else {
+        if (rc == P::R)
+          pipe_bwd_chunk<T, D, 1, true>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[1], rg, li);
+        else
+          pipe_bwd_chunk<T, D, 1, false>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[1], rg, li);
+      }
     } else {
-      if (ten == 0) pipe_fwd_chunk<T, D, MODE, 0>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
-      else pipe_fwd_chunk<T, D, MODE, 1>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
+      if (rc == P::R) {
+        if (ten == 0) pipe_fwd_chunk<T, D, MODE, 0, true>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
+        else pipe_fwd_chunk<T, D, MODE, 1, true>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
+      } else {
+        if (ten == 0) pipe_fwd_chunk<T, D, MODE, 0, false>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
+        else pipe_fwd_chunk<T, D, MODE, 1, false>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
+      }
     }
     // release the slot: order this lane's reads before the next bulk write
     fence_proxy_async_smem();

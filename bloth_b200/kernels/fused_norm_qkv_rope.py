@@ -40,9 +40,8 @@ def norm_rope_backward(dy2, x2, weight, cos2, sin2, rstd):
     half = cos2.shape[-1]
     dx = torch.empty((M, N), dtype=x2.dtype, device=x2.device)
     dw = torch.empty(N, dtype=weight.dtype, device=x2.device)
-    lib = _lib.load()
-    with torch.cuda.device(x2.device):
-        ws_bytes = lib.bloth_norm_rope_bwd_workspace_bytes(M, N, _lib.dtype_code(x2.dtype))
+    ws_bytes = _lib.workspace_bytes("bloth_norm_rope_bwd_workspace_bytes", x2.device, M, N,
+                                    _lib.dtype_code(x2.dtype))
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x2.device)
     rc = _lib.call("bloth_norm_rope_bwd", x2, _lib.ptr(dy2), dy2.stride(0), _lib.ptr(x2),
                    x2.stride(0), _lib.ptr(weight), _lib.ptr(cos2), _lib.ptr(sin2), cos2.stride(0),
@@ -213,10 +212,8 @@ class _QKNormRoPEFunction(torch.autograd.Function):
         dk = None if k4 is None else torch.empty_like(k4, memory_format=torch.contiguous_format)
         dwq = torch.empty(D, dtype=wq.dtype, device=q4.device)
         dwk = None if k4 is None else torch.empty(D, dtype=wk.dtype, device=q4.device)
-        lib = _lib.load()
-        with torch.cuda.device(q4.device):
-            ws_bytes = lib.bloth_qk_norm_rope_bwd_workspace_bytes(B, S, D,
-                                                                 _lib.dtype_code(q4.dtype))
+        ws_bytes = _lib.workspace_bytes("bloth_qk_norm_rope_bwd_workspace_bytes", q4.device, B,
+                                        S, D, _lib.dtype_code(q4.dtype))
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=q4.device)
         rc = _lib.call(
             "bloth_qk_norm_rope_bwd", q4, _lib.ptr(gq), _head_strides(gq), _lib.ptr(gk),

@@ -55,9 +55,8 @@ def rmsnorm_backward(dy2: torch.Tensor, x2: torch.Tensor, weight: torch.Tensor,
     M, N = x2.shape
     dx = torch.empty((M, N), dtype=x2.dtype, device=x2.device)
     dw = torch.empty(N, dtype=weight.dtype, device=x2.device)
-    lib = _lib.load()
-    with torch.cuda.device(x2.device):
-        ws_bytes = lib.bloth_rmsnorm_bwd_workspace_bytes(M, N, _lib.dtype_code(x2.dtype))
+    ws_bytes = _lib.workspace_bytes("bloth_rmsnorm_bwd_workspace_bytes", x2.device, M, N,
+                                    _lib.dtype_code(x2.dtype))
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x2.device)
     rc = _lib.call("bloth_rmsnorm_bwd", x2, _lib.ptr(dy2), dy2.stride(0), _lib.ptr(x2),
                    x2.stride(0), _lib.ptr(weight), _lib.ptr(rstd), _lib.ptr(dx), dx.stride(0),
