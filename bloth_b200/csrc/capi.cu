@@ -85,6 +85,7 @@ cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // ---- per-head validation ----
 bool head_dim_ok(int64_t D) { return D == 64 || D == 128 || D == 256; }
+constexpr int64_t kMaxTokens = (int64_t)1 << 31;  // B*S must stay below this
 
 int check_heads_tensor(const void* p, const int64_t* st, int dtype) {
   if (p == nullptr || st == nullptr) return BLOTH_ERR_NULL;
@@ -304,7 +305,7 @@ int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* 
                            int64_t Hk, int64_t D, float eps, int dtype, int w_dtype, void* stream) {
   if (!is_float_dt(dtype) || !is_float_dt(w_dtype)) return BLOTH_ERR_DTYPE;
   if (!head_dim_ok(D) || B < 0 || S < 0 || Hq < 0 || Hk < 0 || Hq + Hk < 1 || Hq > (1 << 20) ||
-      Hk > (1 << 20))
+      Hk > (1 << 20) || (S > 0 && B >= kMaxTokens / S))
     return BLOTH_ERR_SHAPE;
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -364,7 +365,7 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
                            void* stream) {
   if (!is_float_dt(dtype) || !is_float_dt(w_dtype)) return BLOTH_ERR_DTYPE;
   if (!head_dim_ok(D) || B < 0 || S < 0 || Hq < 0 || Hk < 0 || Hq + Hk < 1 || Hq > (1 << 20) ||
-      Hk > (1 << 20))
+      Hk > (1 << 20) || (S > 0 && B >= kMaxTokens / S))
     return BLOTH_ERR_SHAPE;
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -415,7 +416,9 @@ int bloth_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* 
                int cs_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int transpose, int dtype,
                void* stream) {
   if (!is_float_dt(dtype)) return BLOTH_ERR_DTYPE;
-  if (!head_dim_ok(D) || B < 0 || S < 0 || H < 1 || H > (1 << 20)) return BLOTH_ERR_SHAPE;
+  if (!head_dim_ok(D) || B < 0 || S < 0 || H < 1 || H > (1 << 20) ||
+      (S > 0 && B >= kMaxTokens / S))
+    return BLOTH_ERR_SHAPE;
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
   a.fault = fault_word();

@@ -31,6 +31,7 @@ enum HeadMode : int { kHeadNormFwd = 0, kHeadRopeFwd = 1, kHeadNormBwd = 2 };
 template <typename T, int D, int MODE>
 struct HP {
   using G = HG<T, D>;
+  using AccT = typename AccOf<T>::type;
   static constexpr bool BWD = MODE == kHeadNormBwd;
   static constexpr int ROWB = D * (int)sizeof(T);            // bytes of one head row
   static constexpr int R = (BWD ? 2048 : 4096) / ROWB;       // rows per chunk and tensor
@@ -38,15 +39,22 @@ struct HP {
   static constexpr int RSTD_OFF = NT * R * ROWB;
   static constexpr bool RSTD_BULK = BWD && (R % 4 == 0);     // rstd rows fill 16-byte units
   static constexpr int SLOT = RSTD_OFF + (BWD ? ((R * 4 + 15) / 16) * 16 : 0);
-  static constexpr int NST = BWD ? 4 : 3;                    // ring slots per warp
-  static constexpr int WPB = BWD ? 12 : 16;                  // warps per CTA
+  static constexpr int NST = BWD ? 3 : 4;                    // ring slots per warp
+  // shared memory of a CTA of `wpb` warps: rings, mbarriers, the fp32 weights
+  // of q and k, and (backward) the q-phase weight-gradient partials per warp
+  static constexpr int smem_for(int wpb) {
+    return wpb * NST * SLOT + wpb * NST * 8 + 2 * D * 4 + (BWD ? wpb * D * (int)sizeof(AccT) : 0);
+  }
+  static constexpr int kSmemMax = 227 * 1024;
+  static constexpr int WPB = !BWD ? 12 : (smem_for(16) <= kSmemMax ? 16 : (smem_for(14) <= kSmemMax ? 14 : 12));
   static constexpr int RING = WPB * NST * SLOT;
   static constexpr int BARS = RING;                          // one mbarrier per slot
   static constexpr int WSM = BARS + WPB * NST * 8;           // q and k weights, fp32 [2][D]
-  static constexpr int SMEM = WSM + 2 * D * 4;
+  static constexpr int REDQ = WSM + 2 * D * 4;               // backward: [WPB][D] q partials
+  static constexpr int SMEM = smem_for(WPB);
   static_assert(R % G::RPW == 0, "chunk rows must fill whole warp steps");
   static_assert(SLOT % 16 == 0, "bulk-copy destinations must be 16-byte aligned");
-  static_assert(SMEM <= 227 * 1024, "ring must fit in shared memory");
+  static_assert(SMEM <= kSmemMax, "ring must fit in shared memory");
 };
 
 // Per-token rotation coefficients of one lane for one tensor (forward):
@@ -161,9 +169,9 @@ __device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned
 // One chunk of the backward: dn = R^T dy = dy_own*cos + dy_partner*sin in
 // the first half (slot 0), dy_own*cos - dy_partner*sin in the second
 // (slot 1); g = dn*w, dx = rstd*(g - xhat*sum(g*xhat)/D), dweight += dn*xhat.
-template <typename T, int D, int TEN, bool FULL>
+template <typename T, int D, bool FULL>
 __device__ __forceinline__ void pipe_bwd_chunk(
-    const HeadArgs& a, const unsigned char* slot, int64_t t, int64_t b, int64_t s, int r0,
+    const HeadArgs& a, int TEN, const unsigned char* slot, int64_t t, int64_t b, int64_t s, int r0,
     int rc, const float (&wo)[HG<T, D>::VPL][HG<T, D>::VEC], const float (&cs)[HG<T, D>::VEC],
     const float (&sn)[HG<T, D>::VEC],
     typename AccOf<T>::type (&acc)[HG<T, D>::VPL][HG<T, D>::VEC], int rg, int li) {
@@ -226,27 +234,24 @@ __device__ __forceinline__ void pipe_bwd_chunk(
   }
 }
 
-// Position of a warp in its chunk sequence: token t = (b, s), chunk j of the
-// token's CT chunks, `left` chunks still to go. Advanced without divisions in
-// the common case (one 32-bit division when a step crosses a sequence).
-struct ChunkCursor {
-  int64_t t, b, s;
-  int j;
-  int64_t left;
-  __device__ __forceinline__ void next(int CT, int64_t W, int64_t S) {
-    --left;
-    if (++j == CT) {
-      j = 0;
-      t += W;
-      s += W;
-      if (s >= S) {
-        const uint32_t q = (uint32_t)((uint64_t)s / (uint64_t)S);
-        b += q;
-        s -= (int64_t)q * S;
-      }
+// Fold a warp's per-lane weight-gradient accumulators of one tensor: add the
+// row groups (lanes with equal li) in a fixed butterfly order, then lanes of
+// row group 0 store the warp's D totals to dst[0..D).
+template <typename T, int D>
+__device__ __forceinline__ void fold_warp_acc(
+    typename AccOf<T>::type (&acc)[HG<T, D>::VPL][HG<T, D>::VEC], typename AccOf<T>::type* dst,
+    int rg, int li) {
+  using G = HG<T, D>;
+#pragma unroll
+  for (int j = 0; j < G::VPL; ++j)
+#pragma unroll
+    for (int e = 0; e < G::VEC; ++e) {
+#pragma unroll
+      for (int o = G::LPR; o < 32; o <<= 1)
+        acc[j][e] += __shfl_xor_sync(0xffffffffu, acc[j][e], o);
+      if (rg == 0) dst[slot_col<T, D>(j, li) + e] = acc[j][e];
     }
-  }
-};
+}
 
 template <typename T, int D, int MODE>
 __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
@@ -285,28 +290,61 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
     }
   }
   __syncthreads();
-  AccT acc[2][G::VPL][G::VEC];
-#pragma unroll
-  for (int q = 0; q < 2; ++q)
-#pragma unroll
-    for (int j = 0; j < G::VPL; ++j)
-#pragma unroll
-      for (int e = 0; e < G::VEC; ++e) acc[q][j][e] = AccT(0);
 
-  const int C0 = (a.H[0] + P::R - 1) / P::R;
-  const int C1 = (a.H[1] + P::R - 1) / P::R;
-  const int CT = C0 + C1;
-  const int64_t ntok = a.B * a.S;
-  const int64_t W = (int64_t)gridDim.x * P::WPB;
-  const int64_t gw = (int64_t)blockIdx.x * P::WPB + warp;
-  const int64_t my_tok = gw < ntok ? (ntok - 1 - gw) / W + 1 : 0;
-  const int64_t nchunk = my_tok * CT;
+  const int C[2] = {(a.H[0] + P::R - 1) / P::R, (a.H[1] + P::R - 1) / P::R};
+  // token counts fit in 32 bits (the host rejects B*S >= 2^31)
+  const int ntok = (int)(a.B * a.S);
+  const int S = (int)a.S;
+  const int W = (int)gridDim.x * P::WPB;
+  const int gw = (int)blockIdx.x * P::WPB + warp;
+  const int my_tok = gw < ntok ? (ntok - 1 - gw) / W + 1 : 0;
+  const int b0 = my_tok > 0 ? gw / S : 0;
+  const int s0 = gw - b0 * S;
 
-  // Issues chunk `c` into ring slot `sl`.
-  auto issue = [&](const ChunkCursor& c, int sl) {
-    const int ten = c.j < C0 ? 0 : 1;
-    const int r0 = (ten == 0 ? c.j : c.j - C0) * P::R;
-    const int rc = min(P::R, a.H[ten] - r0);
+  // Chunk walk. Forward: token-major (a token's q chunks, then its k chunks).
+  // Backward: tensor-major (all of the warp's q chunks, then all its k chunks),
+  // so only one tensor's weights and weight-gradient sums are live at a time.
+  struct Cursor {
+    int t, b, s, ti, left, j, ten;
+  };
+  auto advance = [&](Cursor& c) {
+    --c.left;
+    const int cnt = BWD ? C[c.ten] : C[0] + C[1];
+    if (++c.j < cnt) return;
+    c.j = 0;
+    if (BWD && ++c.ti == my_tok) {  // q phase done: restart the tokens for k
+      c.ti = 0;
+      c.ten = 1;
+      c.t = gw;
+      c.b = b0;
+      c.s = s0;
+      return;
+    }
+    if (!BWD) ++c.ti;
+    c.t += W;
+    c.s += W;
+    if (c.s >= S) {
+      const int q = (int)((unsigned)c.s / (unsigned)S);
+      c.b += q;
+      c.s -= q * S;
+    }
+  };
+  // tensor, first row and row count of the chunk under the cursor
+  auto chunk_of = [&](const Cursor& c, int& ten, int& r0, int& rc) {
+    if (BWD) {
+      ten = c.ten;
+      r0 = c.j * P::R;
+    } else {
+      ten = c.j < C[0] ? 0 : 1;
+      r0 = (ten == 0 ? c.j : c.j - C[0]) * P::R;
+    }
+    rc = min(P::R, a.H[ten] - r0);
+  };
+
+  // Issues the chunk under `c` into ring slot `sl`.
+  auto issue = [&](const Cursor& c, int sl) {
+    int ten, r0, rc;
+    chunk_of(c, ten, r0, rc);
     unsigned char* dst = ring + sl * P::SLOT;
     uint64_t* bar = &bars[sl];
     const bool rstd_copy = P::RSTD_BULK && a.rstd_bulk;
@@ -316,8 +354,8 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
 #pragma unroll
     for (int q = 0; q < P::NT; ++q) {
       const HT& h = q == 0 ? a.src[ten] : a.x[ten];
-      const T* base =
-          reinterpret_cast<const T*>(h.p) + c.b * h.sb + c.s * h.ss + (int64_t)r0 * h.sh;
+      const T* base = reinterpret_cast<const T*>(h.p) + (int64_t)c.b * h.sb +
+                      (int64_t)c.s * h.ss + (int64_t)r0 * h.sh;
       unsigned char* d = dst + q * P::R * P::ROWB;
       if (h.sh == D) {
         if (lane == 0) bulk_load(d, base, (uint32_t)(rc * P::ROWB), bar);
@@ -326,44 +364,66 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
       }
     }
     if (rstd_copy && lane == 0)
-      bulk_load(dst + P::RSTD_OFF, a.rstd_in[ten] + c.t * a.H[ten] + r0, (uint32_t)rc * 4u, bar);
+      bulk_load(dst + P::RSTD_OFF, a.rstd_in[ten] + (int64_t)c.t * a.H[ten] + r0, (uint32_t)rc * 4u,
+                bar);
   };
 
-  ChunkCursor cc;
-  cc.t = gw;
-  cc.b = my_tok > 0 ? gw / a.S : 0;
-  cc.s = gw - cc.b * a.S;
-  cc.j = 0;
-  cc.left = nchunk;
-  ChunkCursor ic = cc;  // issue cursor, NST - 1 chunks ahead
+  const int nchunk = my_tok * (C[0] + C[1]);
+  Cursor cc{gw, b0, s0, 0, nchunk, 0, 0};
+  Cursor ic = cc;  // issue cursor, NST - 1 chunks ahead
   int isl = 0;
   for (int q = 0; q < P::NST - 1 && ic.left > 0; ++q) {
     issue(ic, isl);
-    ic.next(CT, W, a.S);
+    advance(ic);
     isl = isl + 1 == P::NST ? 0 : isl + 1;
   }
 
   float cs[G::VEC], sn[G::VEC];
-  FwdCoef<T, D> kc;                // forward: coefficients of the current tensor and token
-  float wc[G::VPL][G::VEC];        // backward: weights of the current tensor
-  int64_t pos_next = my_tok > 0 ? token_pos<T, D>(a, cc.b, cc.s) : 0;
+  FwdCoef<T, D> kc;          // forward: coefficients of the current tensor and token
+  float wc[G::VPL][G::VEC];  // backward: weights of the current tensor
+  AccT acc[G::VPL][G::VEC];  // backward: weight-gradient sums of the current tensor
+#pragma unroll
+  for (int j = 0; j < G::VPL; ++j)
+#pragma unroll
+    for (int e = 0; e < G::VEC; ++e) acc[j][e] = AccT(0);
+  AccT* redq = reinterpret_cast<AccT*>(smem + P::REDQ) + warp * D;  // backward only
+  int cur_ten = -1;
+  int64_t pos_next = 0;
   const float sgn = a.transpose ? -1.f : 1.f;
   int csl = 0;
   uint32_t cph = 0;
   while (cc.left > 0) {
     if (ic.left > 0) {
       issue(ic, isl);
-      ic.next(CT, W, a.S);
+      advance(ic);
       isl = isl + 1 == P::NST ? 0 : isl + 1;
     }
-    if (cc.j == 0) {
+    int ten, r0, rc;
+    chunk_of(cc, ten, r0, rc);
+    if (BWD && ten != cur_ten) {  // phase start: this tensor's weights, first token's position
+      if (cur_ten == 0) {
+        fold_warp_acc<T, D>(acc, redq, rg, li);
+#pragma unroll
+        for (int j = 0; j < G::VPL; ++j)
+#pragma unroll
+          for (int e = 0; e < G::VEC; ++e) acc[j][e] = AccT(0);
+      }
+      cur_ten = ten;
+      lane_weights<T, D, NORM>(wsm, ten, li, wc);
+      pos_next = token_pos<T, D>(a, cc.b, cc.s);
+    }
+    if (!BWD && cur_ten < 0) {
+      cur_ten = 0;
+      pos_next = token_pos<T, D>(a, cc.b, cc.s);
+    }
+    if (cc.j == 0) {  // token start: cos/sin, and the next token's position
       const int64_t p = pos_next;
-      if (cc.left > CT) {  // the warp has another token: load its position now
-        int64_t s2 = cc.s + W, b2 = cc.b;
-        if (s2 >= a.S) {
-          const uint32_t q = (uint32_t)((uint64_t)s2 / (uint64_t)a.S);
+      if (cc.ti + 1 < my_tok) {
+        int s2 = cc.s + W, b2 = cc.b;
+        if (s2 >= S) {
+          const int q = (int)((unsigned)s2 / (unsigned)S);
           b2 += q;
-          s2 -= (int64_t)q * a.S;
+          s2 -= q * S;
         }
         pos_next = token_pos<T, D>(a, b2, s2);
       }
@@ -373,33 +433,19 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
         for (int e = 0; e < G::VEC; ++e) sn[e] *= sgn;
       }
     }
-    const int ten = cc.j < C0 ? 0 : 1;
-    if (cc.j == 0 || cc.j == C0) {  // new token or switch from q to k: this tensor's weights
-      if constexpr (BWD) {
-        lane_weights<T, D, NORM>(wsm, ten, li, wc);
-      } else {
-        float w[G::VPL][G::VEC];
-        lane_weights<T, D, NORM>(wsm, ten, li, w);
-        make_fwd_coef<T, D>(kc, w, cs, sn);
-      }
+    if (!BWD && (cc.j == 0 || cc.j == C[0])) {  // forward: coefficients of this tensor
+      float w[G::VPL][G::VEC];
+      lane_weights<T, D, NORM>(wsm, ten, li, w);
+      make_fwd_coef<T, D>(kc, w, cs, sn);
     }
-    const int r0 = (ten == 0 ? cc.j : cc.j - C0) * P::R;
-    const int rc = min(P::R, a.H[ten] - r0);
     const bool landed = mbar_wait(&bars[csl], cph, a.fault);
     if (!__all_sync(0xffffffffu, landed)) break;
     const unsigned char* slot = ring + csl * P::SLOT;
     if constexpr (BWD) {
-      if (ten == 0) {
-        if (rc == P::R)
-          pipe_bwd_chunk<T, D, 0, true>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[0], rg, li);
-        else
-          pipe_bwd_chunk<T, D, 0, false>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[0], rg, li);
-      } else {
-        if (rc == P::R)
-          pipe_bwd_chunk<T, D, 1, true>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[1], rg, li);
-        else
-          pipe_bwd_chunk<T, D, 1, false>(a, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc[1], rg, li);
-      }
+      if (rc == P::R)
+        pipe_bwd_chunk<T, D, true>(a, ten, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc, rg, li);
+      else
+        pipe_bwd_chunk<T, D, false>(a, ten, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc, rg, li);
     } else {
       if (rc == P::R) {
         if (ten == 0) pipe_fwd_chunk<T, D, MODE, 0, true>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);
@@ -412,7 +458,7 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
     // release the slot: order this lane's reads before the next bulk write
     fence_proxy_async_smem();
     __syncwarp();
-    cc.next(CT, W, a.S);
+    advance(cc);
     if (++csl == P::NST) {
       csl = 0;
       cph ^= 1u;
@@ -420,28 +466,29 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   }
 
   if constexpr (BWD) {
-    // Weight-gradient partials: fold the row groups of each warp (lanes with
-    // equal li), then the warps of the CTA in a fixed order, through the
-    // (now idle) ring memory.
+    // q partials are in redq; the k partials (or q's, when the warp ended in
+    // the q phase) go to the idle ring memory. Then fold the warps of the CTA
+    // in a fixed order into this CTA's partial row [q D | k D].
     __syncthreads();
-    AccT* red = reinterpret_cast<AccT*>(smem);  // [WPB][2*D]
+    AccT* redk = reinterpret_cast<AccT*>(smem);  // [WPB][D]
+    if (cur_ten == 1) {
+      fold_warp_acc<T, D>(acc, redk + warp * D, rg, li);
+    } else {
+      fold_warp_acc<T, D>(acc, redq, rg, li);  // q phase only (or no tokens)
+      if (rg == 0)
 #pragma unroll
-    for (int q = 0; q < 2; ++q)
+        for (int j = 0; j < G::VPL; ++j)
 #pragma unroll
-      for (int j = 0; j < G::VPL; ++j)
-#pragma unroll
-        for (int e = 0; e < G::VEC; ++e) {
-#pragma unroll
-          for (int o = G::LPR; o < 32; o <<= 1)
-            acc[q][j][e] += __shfl_xor_sync(0xffffffffu, acc[q][j][e], o);
-          if (rg == 0) red[warp * 2 * D + q * D + slot_col<T, D>(j, li) + e] = acc[q][j][e];
-        }
+          for (int e = 0; e < G::VEC; ++e) redk[warp * D + slot_col<T, D>(j, li) + e] = AccT(0);
+    }
     __syncthreads();
+    const AccT* redq0 = reinterpret_cast<const AccT*>(smem + P::REDQ);
     AccT* part = reinterpret_cast<AccT*>(a.partials) + (int64_t)blockIdx.x * 2 * D;
     for (int c = threadIdx.x; c < 2 * D; c += P::WPB * 32) {
+      const AccT* src = c < D ? redq0 + c : redk + (c - D);
       AccT sum = AccT(0);
 #pragma unroll
-      for (int wi = 0; wi < P::WPB; ++wi) sum += red[wi * 2 * D + c];
+      for (int wi = 0; wi < P::WPB; ++wi) sum += src[wi * D];
       part[c] = sum;
     }
   }

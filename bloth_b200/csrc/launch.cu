@@ -120,29 +120,32 @@ int device_fault(int reset) {
   return (int)v;
 }
 
-// Column sums of P accumulator rows of N: CTA x handles 32 columns; warp wi
-// sums rows wi, wi+8, ... in order, then warp 0 adds the 8 warp totals in
-// order, so the result does not depend on scheduling. Columns [0, n0) go to
-// dw0 and [n0, N) to dw1 (skipped when dw1 is NULL), cast to w_dt.
+// Column sums of P accumulator rows of N: CTA x handles 32 columns (one per
+// lane); warp wi of its 32 sums rows wi, wi+32, ... in order, then warp 0 adds
+// the 32 warp totals in order, so the result does not depend on scheduling.
+// Columns [0, n0) go to dw0 and [n0, N) to dw1 (skipped when dw1 is NULL),
+// cast to w_dt.
+constexpr int kReduceWarps = 32;
+
 template <typename AccT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(kReduceWarps * 32)
     dw_reduce_kernel(const AccT* __restrict__ part, int64_t P, int N, void* dw0, int n0, void* dw1,
                      int w_dt) {
-  __shared__ double sm[8][32];
+  __shared__ double sm[kReduceWarps][33];
   const int lane = threadIdx.x & 31;
   const int wi = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
   double s = 0.0;
   if (col < N) {
 #pragma unroll 4
-    for (int64_t p = wi; p < P; p += 8) s += (double)part[p * N + col];
+    for (int64_t p = wi; p < P; p += kReduceWarps) s += (double)part[p * N + col];
   }
   sm[wi][lane] = s;
   __syncthreads();
   if (wi == 0 && col < N) {
     double t = 0.0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) t += sm[i][lane];
+    for (int i = 0; i < kReduceWarps; ++i) t += sm[i][lane];
     const float v = (float)t;
     if (col < n0) st_any(dw0, col, w_dt, v);
     else if (dw1 != nullptr) st_any(dw1, col - n0, w_dt, v);
@@ -154,7 +157,7 @@ int launch_dw_reduce(const AccT* part, int64_t P, int N, void* dw0, int n0, void
                      cudaStream_t st) {
   if (N <= 0) return BLOTH_OK;
   const unsigned grid = (unsigned)((N + 31) / 32);
-  dw_reduce_kernel<AccT><<<grid, 256, 0, st>>>(part, P, N, dw0, n0, dw1, w_dt);
+  dw_reduce_kernel<AccT><<<grid, kReduceWarps * 32, 0, st>>>(part, P, N, dw0, n0, dw1, w_dt);
   return cuda_status(cudaGetLastError());
 }
 
