@@ -138,15 +138,16 @@ __device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned
     partner<T, D>(xp, pf);
     float rstd = 1.f;
     if constexpr (NORM) {
-      float s0 = 0.f, s1 = 0.f;
+      float2 sa = f2(0.f, 0.f), sb = f2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < G::VPL; ++j)
 #pragma unroll
-        for (int e = 0; e < G::VEC; e += 2) {
-          s0 = fmaf(xf[j][e], xf[j][e], s0);
-          s1 = fmaf(xf[j][e + 1], xf[j][e + 1], s1);
+        for (int e = 0; e < G::VEC; e += 4) {
+          const float2 x0 = f2(xf[j][e], xf[j][e + 1]), x1 = f2(xf[j][e + 2], xf[j][e + 3]);
+          sa = f2_fma(x0, x0, sa);
+          sb = f2_fma(x1, x1, sb);
         }
-      const float ss = group_lane_sum<G::LPR>(s0 + s1);
+      const float ss = group_lane_sum<G::LPR>((sa.x + sa.y) + (sb.x + sb.y));
       rstd = rsqrtf(fmaf(ss, kInvD, a.eps));
     }
     if (FULL || rl < rc) {
@@ -154,9 +155,15 @@ __device__ __forceinline__ void pipe_fwd_chunk(const HeadArgs& a, const unsigned
 #pragma unroll
       for (int j = 0; j < G::VPL; ++j) {
         float o[G::VEC];
+        const float2 r2 = f2s(rstd);
 #pragma unroll
-        for (int e = 0; e < G::VEC; ++e)
-          o[e] = fmaf(xf[j][e], k.al[j][e], pf[j][e] * k.be[j][e]) * rstd;
+        for (int e = 0; e < G::VEC; e += 2) {
+          const float2 t = f2_mul(f2(pf[j][e], pf[j][e + 1]), f2(k.be[j][e], k.be[j][e + 1]));
+          const float2 y = f2_mul(
+              f2_fma(f2(xf[j][e], xf[j][e + 1]), f2(k.al[j][e], k.al[j][e + 1]), t), r2);
+          o[e] = y.x;
+          o[e + 1] = y.y;
+        }
         stg_pack<T, G::VEC>(drow + j * G::LPR * G::VEC, pack<T, G::VEC>(o));
       }
       if constexpr (NORM) {
@@ -173,7 +180,7 @@ template <typename T, int D, bool FULL>
 __device__ __forceinline__ void pipe_bwd_chunk(
     const HeadArgs& a, int TEN, const unsigned char* slot, int64_t t, int64_t b, int64_t s, int r0,
     int rc, const float (&wo)[HG<T, D>::VPL][HG<T, D>::VEC], const float (&cs)[HG<T, D>::VEC],
-    const float (&sn)[HG<T, D>::VEC],
+    const float (&sn)[HG<T, D>::VEC], const float (&snn)[HG<T, D>::VEC],
     typename AccOf<T>::type (&acc)[HG<T, D>::VPL][HG<T, D>::VEC], int rg, int li) {
   using G = HG<T, D>;
   using P = HP<T, D, kHeadNormBwd>;
@@ -206,28 +213,52 @@ __device__ __forceinline__ void pipe_bwd_chunk(
     for (int j = 0; j < G::VPL; ++j) unpack(gp[j], gf[j]);
     partner<T, D>(gp, pf);
     float g[G::VPL][G::VEC], xh[G::VPL][G::VEC];
-    float dd[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 da = f2(0.f, 0.f), db = f2(0.f, 0.f);
+    const float2 r2 = f2s(rstd);
 #pragma unroll
     for (int j = 0; j < G::VPL; ++j) {
       float xf[G::VEC];
       unpack(xp[j], xf);
 #pragma unroll
-      for (int e = 0; e < G::VEC; ++e) {
-        const float dn = fmaf(j == 0 ? pf[j][e] : -pf[j][e], sn[e], gf[j][e] * cs[e]);
-        xh[j][e] = xf[e] * rstd;
-        g[j][e] = dn * wo[j][e];
-        dd[e & 3] = fmaf(g[j][e], xh[j][e], dd[e & 3]);
-        if (valid) acc_add(acc[j][e], dn, xh[j][e]);
+      for (int e = 0; e < G::VEC; e += 2) {
+        // slot 0: dn = dy*cos + dy_p*sin; slot 1: dn = dy*cos - dy_p*sin
+        const float2 s2 = j == 0 ? f2(sn[e], sn[e + 1]) : f2(snn[e], snn[e + 1]);
+        const float2 dn = f2_fma(f2(pf[j][e], pf[j][e + 1]), s2,
+                                 f2_mul(f2(gf[j][e], gf[j][e + 1]), f2(cs[e], cs[e + 1])));
+        const float2 x2 = f2_mul(f2(xf[e], xf[e + 1]), r2);
+        const float2 g2 = f2_mul(dn, f2(wo[j][e], wo[j][e + 1]));
+        if ((e / 2) & 1) db = f2_fma(g2, x2, db);
+        else da = f2_fma(g2, x2, da);
+        xh[j][e] = x2.x;
+        xh[j][e + 1] = x2.y;
+        g[j][e] = g2.x;
+        g[j][e + 1] = g2.y;
+        if (valid) {
+          if constexpr (std::is_same<typename AccOf<T>::type, float>::value) {
+            const float2 a2 = f2_fma(dn, x2, f2(acc[j][e], acc[j][e + 1]));
+            acc[j][e] = a2.x;
+            acc[j][e + 1] = a2.y;
+          } else {
+            acc_add(acc[j][e], dn.x, x2.x);
+            acc_add(acc[j][e + 1], dn.y, x2.y);
+          }
+        }
       }
     }
-    const float dot = group_lane_sum<G::LPR>((dd[0] + dd[1]) + (dd[2] + dd[3])) * kInvD;
+    const float dot = group_lane_sum<G::LPR>((da.x + da.y) + (db.x + db.y)) * kInvD;
     if (valid) {
       T* drow = dptr + (int64_t)(u * G::RPW) * dsh;
 #pragma unroll
       for (int j = 0; j < G::VPL; ++j) {
         float o[G::VEC];
+        const float2 nd = f2s(-dot);
 #pragma unroll
-        for (int e = 0; e < G::VEC; ++e) o[e] = rstd * fmaf(-xh[j][e], dot, g[j][e]);
+        for (int e = 0; e < G::VEC; e += 2) {
+          const float2 y = f2_mul(
+              f2_fma(f2(xh[j][e], xh[j][e + 1]), nd, f2(g[j][e], g[j][e + 1])), r2);
+          o[e] = y.x;
+          o[e + 1] = y.y;
+        }
         stg_pack<T, G::VEC>(drow + j * G::LPR * G::VEC, pack<T, G::VEC>(o));
       }
     }
@@ -379,6 +410,7 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   }
 
   float cs[G::VEC], sn[G::VEC];
+  float snn[G::VEC];         // backward: -sin
   FwdCoef<T, D> kc;          // forward: coefficients of the current tensor and token
   float wc[G::VPL][G::VEC];  // backward: weights of the current tensor
   AccT acc[G::VPL][G::VEC];  // backward: weight-gradient sums of the current tensor
@@ -432,6 +464,10 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
 #pragma unroll
         for (int e = 0; e < G::VEC; ++e) sn[e] *= sgn;
       }
+      if constexpr (BWD) {
+#pragma unroll
+        for (int e = 0; e < G::VEC; ++e) snn[e] = -sn[e];
+      }
     }
     if (!BWD && (cc.j == 0 || cc.j == C[0])) {  // forward: coefficients of this tensor
       float w[G::VPL][G::VEC];
@@ -443,9 +479,9 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
     const unsigned char* slot = ring + csl * P::SLOT;
     if constexpr (BWD) {
       if (rc == P::R)
-        pipe_bwd_chunk<T, D, true>(a, ten, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc, rg, li);
+        pipe_bwd_chunk<T, D, true>(a, ten, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, snn, acc, rg, li);
       else
-        pipe_bwd_chunk<T, D, false>(a, ten, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, acc, rg, li);
+        pipe_bwd_chunk<T, D, false>(a, ten, slot, cc.t, cc.b, cc.s, r0, rc, wc, cs, sn, snn, acc, rg, li);
     } else {
       if (rc == P::R) {
         if (ten == 0) pipe_fwd_chunk<T, D, MODE, 0, true>(a, slot, cc.t, cc.b, cc.s, r0, rc, kc, rg, li);

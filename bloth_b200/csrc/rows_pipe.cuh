@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
     if constexpr (!BWD) {
       const unsigned char* rowp = slot + (size_t)grp * pp.row_bytes;
       Pack<T, VEC> xp[VPT];
-      float s0 = 0.f, s1 = 0.f;
+      float2 sa = f2(0.f, 0.f), sb = f2(0.f, 0.f);
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int c = (j * TPR + lt) * VEC;
@@ -228,12 +228,13 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
         float f[VEC];
         unpack(xp[j], f);
 #pragma unroll
-        for (int e = 0; e < VEC; ++e) {
-          if (e & 1) s1 = fmaf(f[e], f[e], s1);
-          else s0 = fmaf(f[e], f[e], s0);
+        for (int e = 0; e < VEC; e += 2) {
+          const float2 x2 = f2(f[e], f[e + 1]);
+          if ((e / 2) & 1) sb = f2_fma(x2, x2, sb);
+          else sa = f2_fma(x2, x2, sa);
         }
       }
-      const float ss = RR::sum(s0 + s1, red, grp, lt, parity);
+      const float ss = RR::sum((sa.x + sa.y) + (sb.x + sb.y), red, grp, lt, parity);
       const float rstd = rsqrtf(ss * inv_n + a.eps);
       if (valid) {
         if (lt == 0) a.rstd_out[row] = rstd;
@@ -244,8 +245,13 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
           if (c < N) {
             float f[VEC];
             unpack(xp[j], f);
+            const float2 r2 = f2s(rstd);
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) f[e] = f[e] * rstd * wr[j][e];
+            for (int e = 0; e < VEC; e += 2) {
+              const float2 y = f2_mul(f2_mul(f2(f[e], f[e + 1]), r2), f2(wr[j][e], wr[j][e + 1]));
+              f[e] = y.x;
+              f[e + 1] = y.y;
+            }
             if constexpr (ROPE) rope_pipe_fwd<T, VEC>(f, c, rowp, rstd, a, row);
             stg_pack<T, VEC>(yr + c, pack<T, VEC>(f));
           }
@@ -256,7 +262,8 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
       const unsigned char* xrp = slot + (size_t)(RPC + grp) * pp.row_bytes;
       const float rstd = rstd_in;
       // pass 1: dot = sum(dn*w*xhat), dweight terms dn*xhat
-      float d0 = 0.f, d1 = 0.f;
+      float2 da = f2(0.f, 0.f), db = f2(0.f, 0.f);
+      const float2 r2 = f2s(rstd);
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int c = (j * TPR + lt) * VEC;
@@ -266,15 +273,24 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
           unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
           if constexpr (ROPE) rope_pipe_bwd<T, VEC>(dn, c, dyp, a, row);
 #pragma unroll
-          for (int e = 0; e < VEC; ++e) {
-            const float xh = xf[e] * rstd;
-            if (e & 1) d1 = fmaf(dn[e] * wr[j][e], xh, d1);
-            else d0 = fmaf(dn[e] * wr[j][e], xh, d0);
-            acc_fma(acc[j][e], dn[e], xh);
+          for (int e = 0; e < VEC; e += 2) {
+            const float2 d2 = f2(dn[e], dn[e + 1]);
+            const float2 x2 = f2_mul(f2(xf[e], xf[e + 1]), r2);
+            const float2 t = f2_mul(d2, f2(wr[j][e], wr[j][e + 1]));
+            if ((e / 2) & 1) db = f2_fma(t, x2, db);
+            else da = f2_fma(t, x2, da);
+            if constexpr (std::is_same<AccT, float>::value) {
+              const float2 a2 = f2_fma(d2, x2, f2(acc[j][e], acc[j][e + 1]));
+              acc[j][e] = a2.x;
+              acc[j][e + 1] = a2.y;
+            } else {
+              acc_fma(acc[j][e], d2.x, x2.x);
+              acc_fma(acc[j][e + 1], d2.y, x2.y);
+            }
           }
         }
       }
-      const float dot = RR::sum(d0 + d1, red, grp, lt, parity) * inv_n;
+      const float dot = RR::sum((da.x + da.y) + (db.x + db.y), red, grp, lt, parity) * inv_n;
       // pass 2: dx = rstd*(dn*w - xhat*dot), dn and xhat re-read from the slot
       if (valid) {
         T* dxr = reinterpret_cast<T*>(a.out) + row * a.ldo;
@@ -286,8 +302,15 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
             unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
             unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
             if constexpr (ROPE) rope_pipe_bwd<T, VEC>(dn, c, dyp, a, row);
+            const float2 nd = f2s(-dot);
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) o[e] = rstd * fmaf(-(xf[e] * rstd), dot, dn[e] * wr[j][e]);
+            for (int e = 0; e < VEC; e += 2) {
+              const float2 x2 = f2_mul(f2(xf[e], xf[e + 1]), r2);
+              const float2 y = f2_mul(
+                  f2_fma(x2, nd, f2_mul(f2(dn[e], dn[e + 1]), f2(wr[j][e], wr[j][e + 1]))), r2);
+              o[e] = y.x;
+              o[e + 1] = y.y;
+            }
             stg_pack<T, VEC>(dxr + c, pack<T, VEC>(o));
           }
         }
