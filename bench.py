@@ -34,6 +34,17 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 METRIC = "fused RMSNorm+RoPE fwd+bwd tokens/s and HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
+
+# DRAM bytes (read + write) of one launch of each C-ABI call at the Llama-3-8B
+# shape, from the ncu captures summarised in profiles/ (cold L2, one launch of
+# the streaming kernel; a backward's dweight reduce launch moves under 1 MB and
+# is not included).
+PROFILED_TRAFFIC = {
+    ("llama3-8b", "bloth_qk_norm_rope_fwd"): 335_869_696 + 285_579_520,
+    ("llama3-8b", "bloth_qk_norm_rope_bwd"): 678_338_048 + 302_838_528,
+    ("llama3-8b", "bloth_rmsnorm_fwd"): 268_482_560 + 216_374_784,
+    ("llama3-8b", "bloth_rmsnorm_bwd"): 537_056_000 + 233_986_816,
+}
 NOMINAL_HBM_GBS = 8000.0
 
 # name -> (batch, seq, hidden (0 = none), heads_q, heads_kv, head_dim, theta, eps, packed)
@@ -292,6 +303,9 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--once", action="store_true",
+                    help="run --warmup steps and one more fwd+bwd step, untimed, and exit "
+                         "(a fixed launch sequence for profilers)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -328,7 +342,7 @@ def main() -> None:
     if world > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
     # tokens this rank processes per step
@@ -336,6 +350,13 @@ def main() -> None:
     tokens_local = b_local * S
     inp = make_inputs(name, b_local, dev, seed=1234 + rank, shard=(rank, world))
     nbytes = step_bytes(tokens_local, name)
+    if args.once:
+        for _ in range(args.warmup + 1):
+            run_step(inp, bloth)
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.destroy_process_group()
+        return
 
     def barrier():
         if dist is not None:
@@ -444,7 +465,9 @@ def main() -> None:
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
                          if "hbm_gbs" in peaks else "fallback 6650 GB/s",
-                         "traffic": None},
+                         "traffic": PROFILED_TRAFFIC.get((name, top[0])),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                           "profiles/ (cold-L2 single launch)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
