@@ -8,16 +8,25 @@ and kernels/__init__.py:7-8):
     kernels.fused_norm_rope, kernels.rope_embedding
 
 plus fused_qk_norm_rope / BlothQKNormRoPE (q and k per-head norm + RoPE in one
-launch, cos/sin from positions in-register). The compute runs in hand-written
+launch, cos/sin from positions in-register or from HF tables), apply_rope_qk /
+apply_rotary_pos_emb (RoPE of q and k in one launch), the (1 + w) weighting of
+Gemma-family norms (weight_offset), and patch_model(..., patch_attention=True),
+which routes HF Qwen3 / Llama / Mistral / Qwen2 attention through them. The compute runs in hand-written
 CUDA behind the C ABI of include/bloth_b200.h; importing this package does not
 touch the GPU, and every op raises if the library or a CUDA device is missing.
 """
 from __future__ import annotations
 
-__version__ = "0.1.0"
+__version__ = "0.2.0"
 
 from . import kernels  # noqa: F401
-from .kernels import fused_norm_rope, fused_qk_norm_rope, apply_rope  # noqa: F401
+from .kernels import (  # noqa: F401
+    apply_rope,
+    apply_rope_qk,
+    apply_rotary_pos_emb,
+    fused_norm_rope,
+    fused_qk_norm_rope,
+)
 from .modules import (  # noqa: F401
     BlothFusedNormQKV,
     BlothQKNormRoPE,
@@ -41,6 +50,8 @@ __all__ = [
     "BlothQKNormRoPE",
     "rope_embedding",
     "apply_rope",
+    "apply_rope_qk",
+    "apply_rotary_pos_emb",
     "BlothRoPE",
     "rope_inv_freq",
     "patch_model",

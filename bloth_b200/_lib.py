@@ -43,27 +43,30 @@ _SIGNATURES = {
     "bloth_strerror": (ctypes.c_char_p, [_int]),
     "bloth_last_cuda_error": (_int, []),
     "bloth_device_fault": (_int, [_int]),
-    "bloth_rmsnorm_fwd": (_int, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _f32, _int, _int, _vp]),
+    "bloth_rmsnorm_fwd": (_int, [_vp, _i64, _vp, _f32, _vp, _i64, _vp, _i64, _i64, _f32, _int,
+                                 _int, _vp]),
     "bloth_rmsnorm_bwd_workspace_bytes": (_sz, [_i64, _i64, _int]),
-    "bloth_rmsnorm_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64, _i64, _int,
-                                 _int, _vp, _sz, _vp]),
-    "bloth_rmsnorm_bwd_noalloc": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _i64,
-                                         _i64, _int, _int, _vp]),
-    "bloth_norm_rope_fwd": (_int, [_vp, _i64, _vp, _vp, _vp, _i64, _int, _i64, _vp, _i64, _vp,
-                                   _i64, _i64, _f32, _int, _int, _vp]),
+    "bloth_rmsnorm_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _f32, _vp, _vp, _i64, _vp, _i64, _i64,
+                                 _int, _int, _vp, _sz, _vp]),
+    "bloth_rmsnorm_bwd_noalloc": (_int, [_vp, _i64, _vp, _i64, _vp, _f32, _vp, _vp, _i64, _vp,
+                                         _i64, _i64, _int, _int, _vp]),
+    "bloth_norm_rope_fwd": (_int, [_vp, _i64, _vp, _f32, _vp, _vp, _i64, _int, _i64, _vp, _i64,
+                                   _vp, _i64, _i64, _f32, _int, _int, _vp]),
     "bloth_norm_rope_bwd_workspace_bytes": (_sz, [_i64, _i64, _int]),
-    "bloth_norm_rope_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _int, _i64, _vp, _vp,
-                                   _i64, _vp, _i64, _i64, _int, _int, _vp, _sz, _vp]),
-    "bloth_qk_norm_rope_fwd": (_int, [_vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p, _vp, _i64p,
-                                      _vp, _vp, _vp, _i64p, _int, _vp, _vp, _vp, _i64p, _i64,
-                                      _int, _i64, _i64, _i64, _i64, _i64, _f32, _int, _int, _vp]),
+    "bloth_norm_rope_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _f32, _vp, _vp, _i64, _int, _i64,
+                                   _vp, _vp, _i64, _vp, _i64, _i64, _int, _int, _vp, _sz, _vp]),
+    "bloth_qk_norm_rope_fwd": (_int, [_vp, _i64p, _vp, _i64p, _vp, _vp, _f32, _vp, _i64p, _vp,
+                                      _i64p, _vp, _vp, _vp, _i64p, _int, _vp, _vp, _vp, _i64p,
+                                      _i64, _int, _f32, _i64, _i64, _i64, _i64, _i64, _f32, _int,
+                                      _int, _vp]),
     "bloth_qk_norm_rope_bwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _int]),
     "bloth_qk_norm_rope_bwd": (_int, [_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _vp,
-                                      _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _vp, _vp, _i64p,
-                                      _int, _vp, _vp, _vp, _i64p, _i64, _int, _i64, _i64, _i64,
-                                      _i64, _i64, _int, _int, _vp, _sz, _vp]),
-    "bloth_rope": (_int, [_vp, _i64p, _vp, _i64p, _vp, _i64p, _int, _vp, _vp, _vp, _i64p, _i64,
-                          _int, _i64, _i64, _i64, _i64, _int, _int, _vp]),
+                                      _f32, _vp, _vp, _vp, _i64p, _vp, _i64p, _vp, _vp, _vp,
+                                      _i64p, _int, _vp, _vp, _vp, _i64p, _i64, _int, _f32, _i64,
+                                      _i64, _i64, _i64, _i64, _int, _int, _vp, _sz, _vp]),
+    "bloth_rope": (_int, [_vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _vp, _i64p, _int, _vp,
+                          _vp, _vp, _i64p, _i64, _int, _f32, _i64, _i64, _i64, _i64, _i64, _int,
+                          _int, _vp]),
 }
 
 

@@ -16,7 +16,7 @@ using namespace bloth;
 
 namespace {
 
-constexpr int kVersion = (0 << 16) | (1 << 8) | 0;
+constexpr int kVersion = (0 << 16) | (2 << 8) | 0;
 
 bool is_float_dt(int dt) { return dt == BLOTH_F32 || dt == BLOTH_BF16 || dt == BLOTH_F16; }
 int elem_size(int dt) { return dt == BLOTH_F32 ? 4 : 2; }
@@ -69,7 +69,7 @@ int check_rope_table(const void* cos, const void* sin, int64_t ldcs, int cs_dtyp
   return BLOTH_OK;
 }
 
-RowArgs make_rows(int64_t M, int64_t N, float eps, const void* w, int w_dtype) {
+RowArgs make_rows(int64_t M, int64_t N, float eps, const void* w, float w_offset, int w_dtype) {
   RowArgs a;
   std::memset(&a, 0, sizeof(a));
   a.M = M;
@@ -78,6 +78,7 @@ RowArgs make_rows(int64_t M, int64_t N, float eps, const void* w, int w_dtype) {
   a.w = w;
   a.w_dt = w_dtype;
   a.w_vec = aligned(w, 16) ? 1 : 0;
+  a.w_off = w_offset;
   return a;
 }
 
@@ -108,9 +109,10 @@ HT make_ht(const void* p, const int64_t* st) {
 // Position and cos/sin source shared by the per-head entry points.
 int fill_rope_source(HeadArgs& a, const void* pos, const int64_t* pos_strides, int pos_dtype,
                      const float* inv_freq, const void* cos, const void* sin,
-                     const int64_t* cs_strides, int64_t cs_rows, int cs_dtype, int dtype,
-                     int64_t D) {
+                     const int64_t* cs_strides, int64_t cs_rows, int cs_dtype,
+                     float rope_scale, int dtype, int64_t D) {
   a.pos = pos;
+  a.cs_scale = rope_scale;
   if (pos != nullptr) {
     if (pos_dtype != BLOTH_I64 && pos_dtype != BLOTH_I32) return BLOTH_ERR_DTYPE;
     if (pos_strides == nullptr) return BLOTH_ERR_NULL;
@@ -165,7 +167,8 @@ int bloth_last_cuda_error(void) { return bloth::last_cuda_error(); }
 int bloth_device_fault(int reset) { return bloth::device_fault(reset); }
 
 // ---------------------------------------------------------------- RMSNorm
-int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy,
+int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, float w_offset, void* y,
+                      int64_t ldy,
                       float* rstd, int64_t M, int64_t N, float eps, int dtype, int w_dtype,
                       void* stream) {
   int rc = check_rows(M, N, dtype, w_dtype);
@@ -175,7 +178,7 @@ int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_
   if ((rc = check_ld(M, N, {ldx, ldy}))) return rc;
   const bool vec = rows_vec_ok(dtype, N, {x, y}, {ldx, ldy});
   if (!vec && N > kMaxScalarRow) return BLOTH_ERR_ALIGN;
-  RowArgs a = make_rows(M, N, eps, w, w_dtype);
+  RowArgs a = make_rows(M, N, eps, w, w_offset, w_dtype);
   a.x = x;
   a.ldx = ldx;
   a.out = y;
@@ -197,7 +200,7 @@ size_t bloth_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N, int dtype) {
 }
 
 int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
-                      const float* rstd, void* dx, int64_t lddx, void* dw, int64_t M, int64_t N,
+                      float w_offset, const float* rstd, void* dx, int64_t lddx, void* dw, int64_t M, int64_t N,
                       int dtype, int w_dtype, void* workspace, size_t workspace_bytes,
                       void* stream) {
   int rc = check_rows(M, N, dtype, w_dtype);
@@ -207,7 +210,7 @@ int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, 
   if ((rc = check_ld(M, N, {lddy, ldx, lddx}))) return rc;
   const bool vec = rows_vec_ok(dtype, N, {dy, x, dx}, {lddy, ldx, lddx});
   if (!vec && N > kMaxScalarRow) return BLOTH_ERR_ALIGN;
-  RowArgs a = make_rows(M, N, 0.f, w, w_dtype);
+  RowArgs a = make_rows(M, N, 0.f, w, w_offset, w_dtype);
   a.dy = dy;
   a.lddy = lddy;
   a.x = x;
@@ -221,7 +224,7 @@ int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, 
 }
 
 // ------------------------------------------------- fused RMSNorm + RoPE (table)
-int bloth_norm_rope_fwd(const void* x, int64_t ldx, const void* w, const void* cos,
+int bloth_norm_rope_fwd(const void* x, int64_t ldx, const void* w, float w_offset, const void* cos,
                         const void* sin, int64_t ldcs, int cs_dtype, int64_t half, void* y,
                         int64_t ldy, float* rstd, int64_t M, int64_t N, float eps, int dtype,
                         int w_dtype, void* stream) {
@@ -233,7 +236,7 @@ int bloth_norm_rope_fwd(const void* x, int64_t ldx, const void* w, const void* c
   if ((rc = check_ld(M, N, {ldx, ldy}))) return rc;
   const bool vec = rows_vec_ok(dtype, N, {x, y}, {ldx, ldy});
   if (!vec && N > kMaxScalarRow) return BLOTH_ERR_ALIGN;
-  RowArgs a = make_rows(M, N, eps, w, w_dtype);
+  RowArgs a = make_rows(M, N, eps, w, w_offset, w_dtype);
   a.x = x;
   a.ldx = ldx;
   a.out = y;
@@ -262,7 +265,7 @@ size_t bloth_norm_rope_bwd_workspace_bytes(int64_t M, int64_t N, int dtype) {
 }
 
 int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
-                        const void* cos, const void* sin, int64_t ldcs, int cs_dtype,
+                        float w_offset, const void* cos, const void* sin, int64_t ldcs, int cs_dtype,
                         int64_t half, const float* rstd, void* dx, int64_t lddx, void* dw,
                         int64_t M, int64_t N, int dtype, int w_dtype, void* workspace,
                         size_t workspace_bytes, void* stream) {
@@ -274,7 +277,7 @@ int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx
   if ((rc = check_ld(M, N, {lddy, ldx, lddx}))) return rc;
   const bool vec = rows_vec_ok(dtype, N, {dy, x, dx}, {lddy, ldx, lddx});
   if (!vec && N > kMaxScalarRow) return BLOTH_ERR_ALIGN;
-  RowArgs a = make_rows(M, N, 0.f, w, w_dtype);
+  RowArgs a = make_rows(M, N, 0.f, w, w_offset, w_dtype);
   a.dy = dy;
   a.lddy = lddy;
   a.x = x;
@@ -296,12 +299,13 @@ int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx
 
 // ------------------------------------------------------ per-head q/k kernels
 int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* k,
-                           const int64_t* k_strides, const void* wq, const void* wk, void* q_out,
-                           const int64_t* qo_strides, void* k_out, const int64_t* ko_strides,
-                           float* rstd_q, float* rstd_k, const void* pos,
-                           const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
-                           const void* cos, const void* sin, const int64_t* cs_strides,
-                           int64_t cs_rows, int cs_dtype, int64_t B, int64_t S, int64_t Hq,
+                           const int64_t* k_strides, const void* wq, const void* wk,
+                           float w_offset, void* q_out, const int64_t* qo_strides, void* k_out,
+                           const int64_t* ko_strides, float* rstd_q, float* rstd_k,
+                           const void* pos, const int64_t* pos_strides, int pos_dtype,
+                           const float* inv_freq, const void* cos, const void* sin,
+                           const int64_t* cs_strides, int64_t cs_rows, int cs_dtype,
+                           float rope_scale, int64_t B, int64_t S, int64_t Hq,
                            int64_t Hk, int64_t D, float eps, int dtype, int w_dtype, void* stream) {
   if (!is_float_dt(dtype) || !is_float_dt(w_dtype)) return BLOTH_ERR_DTYPE;
   if (!head_dim_ok(D) || B < 0 || S < 0 || Hq < 0 || Hk < 0 || Hq + Hk < 1 || Hq > (1 << 20) ||
@@ -311,7 +315,7 @@ int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* 
   std::memset(&a, 0, sizeof(a));
   a.fault = fault_word();
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
-                            cs_rows, cs_dtype, dtype, D);
+                            cs_rows, cs_dtype, rope_scale, dtype, D);
   if (rc) return rc;
   if (B * S == 0) return BLOTH_OK;
   const void* src[2] = {q, k};
@@ -334,6 +338,7 @@ int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* 
     a.H[t] = (int)H[t];
   }
   a.w_dt = w_dtype;
+  a.w_off = w_offset;
   a.B = B;
   a.S = S;
   a.eps = eps;
@@ -355,12 +360,14 @@ size_t bloth_qk_norm_rope_bwd_workspace_bytes(int64_t B, int64_t S, int64_t D, i
 int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const void* dk_out,
                            const int64_t* dko_strides, const void* q, const int64_t* q_strides,
                            const void* k, const int64_t* k_strides, const void* wq,
-                           const void* wk, const float* rstd_q, const float* rstd_k, void* dq,
+                           const void* wk, float w_offset, const float* rstd_q,
+                           const float* rstd_k, void* dq,
                            const int64_t* dq_strides, void* dk, const int64_t* dk_strides,
                            void* dwq, void* dwk, const void* pos, const int64_t* pos_strides,
                            int pos_dtype, const float* inv_freq, const void* cos,
                            const void* sin, const int64_t* cs_strides, int64_t cs_rows,
-                           int cs_dtype, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
+                           int cs_dtype, float rope_scale, int64_t B, int64_t S, int64_t Hq,
+                           int64_t Hk, int64_t D,
                            int dtype, int w_dtype, void* workspace, size_t workspace_bytes,
                            void* stream) {
   if (!is_float_dt(dtype) || !is_float_dt(w_dtype)) return BLOTH_ERR_DTYPE;
@@ -371,7 +378,7 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
   std::memset(&a, 0, sizeof(a));
   a.fault = fault_word();
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
-                            cs_rows, cs_dtype, dtype, D);
+                            cs_rows, cs_dtype, rope_scale, dtype, D);
   if (rc) return rc;
   const void* g[2] = {dq_out, dk_out};
   const int64_t* gst[2] = {dqo_strides, dko_strides};
@@ -400,6 +407,7 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
     a.rstd_in[t] = rs[t];
   }
   a.w_dt = w_dtype;
+  a.w_off = w_offset;
   a.B = B;
   a.S = S;
   a.rstd_bulk = (Hq % 4 == 0) && (Hk % 4 == 0) && aligned(rstd_q, 16) &&
@@ -410,28 +418,36 @@ int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const
   });
 }
 
-int bloth_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_strides,
+int bloth_rope(const void* q, const int64_t* q_strides, void* q_out, const int64_t* qo_strides,
+               const void* k, const int64_t* k_strides, void* k_out, const int64_t* ko_strides,
                const void* pos, const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
                const void* cos, const void* sin, const int64_t* cs_strides, int64_t cs_rows,
-               int cs_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int transpose, int dtype,
-               void* stream) {
+               int cs_dtype, float rope_scale, int64_t B, int64_t S, int64_t Hq, int64_t Hk,
+               int64_t D, int transpose, int dtype, void* stream) {
   if (!is_float_dt(dtype)) return BLOTH_ERR_DTYPE;
-  if (!head_dim_ok(D) || B < 0 || S < 0 || H < 1 || H > (1 << 20) ||
-      (S > 0 && B >= kMaxTokens / S))
+  if (!head_dim_ok(D) || B < 0 || S < 0 || Hq < 0 || Hk < 0 || Hq + Hk < 1 || Hq > (1 << 20) ||
+      Hk > (1 << 20) || (S > 0 && B >= kMaxTokens / S))
     return BLOTH_ERR_SHAPE;
   HeadArgs a;
   std::memset(&a, 0, sizeof(a));
   a.fault = fault_word();
   int rc = fill_rope_source(a, pos, pos_strides, pos_dtype, inv_freq, cos, sin, cs_strides,
-                            cs_rows, cs_dtype, dtype, D);
+                            cs_rows, cs_dtype, rope_scale, dtype, D);
   if (rc) return rc;
   if (B * S == 0) return BLOTH_OK;
-  if ((rc = check_heads_tensor(x, x_strides, dtype))) return rc;
-  if ((rc = check_heads_tensor(y, y_strides, dtype))) return rc;
-  a.src[0] = make_ht(x, x_strides);
-  a.dst[0] = make_ht(y, y_strides);
-  a.H[0] = (int)H;
-  a.H[1] = 0;
+  const void* src[2] = {q, k};
+  const int64_t* sst[2] = {q_strides, k_strides};
+  void* dst[2] = {q_out, k_out};
+  const int64_t* dstst[2] = {qo_strides, ko_strides};
+  const int64_t H[2] = {Hq, Hk};
+  for (int t = 0; t < 2; ++t) {
+    if (H[t] == 0) continue;
+    if ((rc = check_heads_tensor(src[t], sst[t], dtype))) return rc;
+    if ((rc = check_heads_tensor(dst[t], dstst[t], dtype))) return rc;
+    a.src[t] = make_ht(src[t], sst[t]);
+    a.dst[t] = make_ht(dst[t], dstst[t]);
+    a.H[t] = (int)H[t];
+  }
   a.B = B;
   a.S = S;
   a.transpose = transpose ? 1 : 0;

@@ -40,6 +40,7 @@ struct HeadArgs {
   HT dst[2];  // forward: q_out, k_out.  backward: dq, dk
   const void* w[2];
   int w_dt;
+  float w_off;  // added to every weight: 1 for (1 + w) norms (Gemma), else 0
   int H[2];
   float* rstd_out[2];
   const float* rstd_in[2];
@@ -54,6 +55,7 @@ struct HeadArgs {
   int cs_vec;
   int64_t cs_sb, cs_sp;
   int64_t cs_rows;  // rows of a table indexed by position; p is clamped to [0, cs_rows)
+  float cs_scale;   // cos and sin are multiplied by this (HF attention_scaling)
   int64_t B, S;
   float eps;
   int transpose;  // RoPE-only: apply R^T
@@ -128,6 +130,11 @@ __device__ __forceinline__ void token_cos_sin(const HeadArgs& a, int64_t b, int6
       cs[e] = __shfl_sync(0xffffffffu, cv[e % G::APL], src);
       sn[e] = __shfl_sync(0xffffffffu, sv[e % G::APL], src);
     }
+  }
+#pragma unroll
+  for (int e = 0; e < G::VEC; ++e) {
+    cs[e] *= a.cs_scale;
+    sn[e] *= a.cs_scale;
   }
   (void)lane;
 }

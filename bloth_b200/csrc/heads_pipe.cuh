@@ -317,7 +317,7 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   if constexpr (NORM) {
     for (int c = threadIdx.x; c < 2 * D; c += P::WPB * 32) {
       const int q = c / D;
-      wsm[c] = a.H[q] != 0 ? ld_any(a.w[q], c - q * D, a.w_dt) : 0.f;
+      wsm[c] = a.H[q] != 0 ? ld_any(a.w[q], c - q * D, a.w_dt) + a.w_off : 0.f;
     }
   }
   __syncthreads();

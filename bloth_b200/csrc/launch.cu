@@ -74,21 +74,26 @@ int occupancy(const void* func, int block, size_t smem) {
   return n;
 }
 
+// The attribute is a ceiling per kernel and device: setting it lowers it as
+// well as raising it, so it is only ever raised (to the largest size any call
+// has asked for), never set back to a smaller request, which would make a
+// later launch with a larger, already-seen size fail.
 int prepare_smem(const void* func, size_t smem) {
-  using Key = std::tuple<int, const void*, size_t>;
+  using Key = std::tuple<int, const void*>;
   static std::mutex mu;
-  static std::set<Key> done;
+  static std::map<Key, size_t> ceiling;
   const int dev = current_device();
-  const Key key{dev, func, smem};
-  {
-    std::lock_guard<std::mutex> lk(mu);
-    if (done.count(key)) return BLOTH_OK;
-  }
+  const Key key{dev, func};
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = ceiling.find(key);
+  if (it != ceiling.end() && it->second >= smem) return BLOTH_OK;
   const cudaError_t e =
       cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return cuda_status(e);
-  std::lock_guard<std::mutex> lk(mu);
-  done.insert(key);
+  if (e != cudaSuccess) {
+    cudaGetLastError();  // do not leave the error for the next launch check
+    return cuda_status(e);
+  }
+  ceiling[key] = smem;
   return BLOTH_OK;
 }
 

@@ -26,7 +26,7 @@
 
 // The entry point with the caller-provided workspace (capi.cu).
 extern "C" int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx,
-                                 const void* w, const float* rstd, void* dx, int64_t lddx,
+                                 const void* w, float w_offset, const float* rstd, void* dx, int64_t lddx,
                                  void* dw, int64_t M, int64_t N, int dtype, int w_dtype,
                                  void* workspace, size_t workspace_bytes, void* stream);
 extern "C" size_t bloth_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N, int dtype);
@@ -62,7 +62,8 @@ void* scratch_address(int* status) {
 }  // namespace
 
 extern "C" int bloth_rmsnorm_bwd_noalloc(const void* dy, int64_t lddy, const void* x,
-                                         int64_t ldx, const void* w, const float* rstd, void* dx,
+                                         int64_t ldx, const void* w, float w_offset,
+                                         const float* rstd, void* dx,
                                          int64_t lddx, void* dw, int64_t M, int64_t N, int dtype,
                                          int w_dtype, void* stream) {
   // Same partial-sum layout as bloth_rmsnorm_bwd, so the results are the same.
@@ -71,6 +72,6 @@ extern "C" int bloth_rmsnorm_bwd_noalloc(const void* dy, int64_t lddy, const voi
   int status = BLOTH_OK;
   void* scratch = scratch_address(&status);
   if (scratch == nullptr) return status;
-  return bloth_rmsnorm_bwd(dy, lddy, x, ldx, w, rstd, dx, lddx, dw, M, N, dtype, w_dtype, scratch,
+  return bloth_rmsnorm_bwd(dy, lddy, x, ldx, w, w_offset, rstd, dx, lddx, dw, M, N, dtype, w_dtype, scratch,
                            (size_t)BLOTH_NOALLOC_SCRATCH_BYTES, stream);
 }

@@ -33,6 +33,7 @@ struct RowArgs {
   const void* w;
   int w_dt;
   int w_vec;  // w aligned for VEC-wide loads
+  float w_off;  // added to every weight: 1 for (1 + w) norms (Gemma), else 0
   float* rstd_out;      // forward
   const float* rstd_in; // backward
   void* partials;       // backward: [gridDim.x][N] accumulator rows
@@ -46,6 +47,19 @@ struct RowArgs {
   int N;
   float eps;
 };
+
+// Weight of column c as the kernels apply it, w[c] + w_off, in fp32.
+__device__ __forceinline__ float ld_weight(const RowArgs& a, int64_t c) {
+  return ld_any(a.w, c, a.w_dt) + a.w_off;
+}
+
+template <int VEC>
+__device__ __forceinline__ void ld_weight_vec(const RowArgs& a, int64_t c, bool vec_ok,
+                                              float (&w)[VEC]) {
+  ld_any_vec<VEC>(a.w, c, a.w_dt, vec_ok, w);
+#pragma unroll
+  for (int e = 0; e < VEC; ++e) w[e] += a.w_off;
+}
 
 template <int TPR, int RPC>
 struct RowReduce {
@@ -82,7 +96,7 @@ __device__ __noinline__ float rope_scalar_fwd(float own, int64_t cc, const T* xr
   const bool first = cc < h;
   const int64_t pc = first ? cc + h : cc - h;
   const int64_t i = first ? cc : cc - h;
-  const float np = to_f(xr[pc]) * rstd * ld_any(a.w, pc, a.w_dt);
+  const float np = to_f(xr[pc]) * rstd * ld_weight(a, pc);
   const float cs = ld_any(a.cos, row * a.ldcs + i, a.cs_dt);
   const float sn = ld_any(a.sin, row * a.ldcs + i, a.cs_dt);
   return first ? (own * cs - np * sn) : (np * sn + own * cs);
@@ -117,7 +131,7 @@ __device__ __forceinline__ void rope_rows_fwd(float (&o)[VEC], int c, const T* x
     const int64_t i = first ? c : c - h;
     float xp[VEC], wp[VEC], cs[VEC], sn[VEC];
     unpack(ldg_pack<T, VEC>(xr + pc), xp);
-    ld_any_vec<VEC>(a.w, pc, a.w_dt, a.w_vec, wp);
+    ld_weight_vec<VEC>(a, pc, a.w_vec, wp);
     ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, true, cs);
     ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, true, sn);
 #pragma unroll
@@ -205,7 +219,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_fwd_ke
       if (c < N) {
         float f[VEC], w[VEC];
         unpack(xp[j], f);
-        ld_any_vec<VEC>(a.w, c, a.w_dt, wv, w);
+        ld_weight_vec<VEC>(a, c, wv, w);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) f[e] = f[e] * rstd * w[e];
         if constexpr (ROPE) rope_rows_fwd<T, VEC>(f, c, xr, rstd, a, row);
@@ -272,7 +286,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_ke
         unpack(dp[j], dn);
         unpack(xp[j], xf);
         if constexpr (ROPE) rope_rows_bwd<T, VEC>(dn, c, dyr, a, row);
-        ld_any_vec<VEC>(a.w, c, a.w_dt, wv, w);
+        ld_weight_vec<VEC>(a, c, wv, w);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) {
           const float xh = xf[e] * rstd;
@@ -294,7 +308,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_ke
         unpack(dp[j], dn);
         unpack(xp[j], xf);
         if constexpr (ROPE) rope_rows_bwd<T, VEC>(dn, c, dyr, a, row);
-        ld_any_vec<VEC>(a.w, c, a.w_dt, wv, w);
+        ld_weight_vec<VEC>(a, c, wv, w);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) o[e] = rstd * (dn[e] * w[e] - (xf[e] * rstd) * dot);
         stg_pack<T, VEC>(dxr + c, pack<T, VEC>(o));

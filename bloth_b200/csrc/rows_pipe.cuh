@@ -54,7 +54,7 @@ __device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsi
     const int64_t i = first ? c : c - h;
     float xp[VEC], wp[VEC], cs[VEC], sn[VEC];
     unpack(lds_pack<T, VEC>(rowp + pc * (int64_t)sizeof(T)), xp);
-    ld_any_vec<VEC>(a.w, pc, a.w_dt, a.w_vec, wp);
+    ld_weight_vec<VEC>(a, pc, a.w_vec, wp);
     ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, true, cs);
     ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, true, sn);
 #pragma unroll
@@ -71,7 +71,7 @@ __device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsi
         const bool first = cc < h;
         const int64_t pc = first ? cc + h : cc - h;
         const int64_t i = first ? cc : cc - h;
-        const float np = to_f(xr[pc]) * rstd * ld_any(a.w, pc, a.w_dt);
+        const float np = to_f(xr[pc]) * rstd * ld_weight(a, pc);
         const float cs = ld_any(a.cos, row * a.ldcs + i, a.cs_dt);
         const float sn = ld_any(a.sin, row * a.ldcs + i, a.cs_dt);
         o[e] = first ? (o[e] * cs - np * sn) : (np * sn + o[e] * cs);
@@ -139,7 +139,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
   for (int j = 0; j < VPT; ++j) {
     const int c = (j * TPR + lt) * VEC;
     if (c < N) {
-      ld_any_vec<VEC>(a.w, c, a.w_dt, wv, wr[j]);
+      ld_weight_vec<VEC>(a, c, wv, wr[j]);
     } else {
 #pragma unroll
       for (int e = 0; e < VEC; ++e) wr[j][e] = 0.f;

@@ -6,7 +6,7 @@ Same names as the reference's ``bloth.kernels`` package for this path
 """
 from .rms_norm import bloth_rms_norm, rms_norm  # noqa: F401
 from .fused_norm_qkv_rope import fused_norm_rope, fused_qk_norm_rope  # noqa: F401
-from .rope import apply_rope, rope_embedding  # noqa: F401
+from .rope import apply_rope, apply_rope_qk, apply_rotary_pos_emb, rope_embedding  # noqa: F401
 
 __all__ = [
     "bloth_rms_norm",
@@ -14,5 +14,7 @@ __all__ = [
     "fused_norm_rope",
     "fused_qk_norm_rope",
     "apply_rope",
+    "apply_rope_qk",
+    "apply_rotary_pos_emb",
     "rope_embedding",
 ]

@@ -22,20 +22,20 @@ from .rms_norm import _as_rows, _check_row
 
 
 # ---------------------------------------------------------------- row tables
-def norm_rope_forward(x2, weight, cos2, sin2, eps):
+def norm_rope_forward(x2, weight, cos2, sin2, eps, weight_offset=0.0):
     M, N = x2.shape
     half = cos2.shape[-1]
     y = torch.empty((M, N), dtype=x2.dtype, device=x2.device)
     rstd = torch.empty(M, dtype=torch.float32, device=x2.device)
     rc = _lib.call("bloth_norm_rope_fwd", x2, _lib.ptr(x2), x2.stride(0), _lib.ptr(weight),
-                   _lib.ptr(cos2), _lib.ptr(sin2), cos2.stride(0), _lib.dtype_code(cos2.dtype),
+                   float(weight_offset), _lib.ptr(cos2), _lib.ptr(sin2), cos2.stride(0), _lib.dtype_code(cos2.dtype),
                    half, _lib.ptr(y), y.stride(0), _lib.ptr(rstd), M, N, float(eps),
                    _lib.dtype_code(x2.dtype), _lib.dtype_code(weight.dtype), _lib.stream_of(x2))
     _lib.check(rc, "fused norm+rope forward")
     return y, rstd
 
 
-def norm_rope_backward(dy2, x2, weight, cos2, sin2, rstd):
+def norm_rope_backward(dy2, x2, weight, cos2, sin2, rstd, weight_offset=0.0):
     M, N = x2.shape
     half = cos2.shape[-1]
     dx = torch.empty((M, N), dtype=x2.dtype, device=x2.device)
@@ -44,7 +44,8 @@ def norm_rope_backward(dy2, x2, weight, cos2, sin2, rstd):
                                     _lib.dtype_code(x2.dtype))
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x2.device)
     rc = _lib.call("bloth_norm_rope_bwd", x2, _lib.ptr(dy2), dy2.stride(0), _lib.ptr(x2),
-                   x2.stride(0), _lib.ptr(weight), _lib.ptr(cos2), _lib.ptr(sin2), cos2.stride(0),
+                   x2.stride(0), _lib.ptr(weight), float(weight_offset), _lib.ptr(cos2),
+                   _lib.ptr(sin2), cos2.stride(0),
                    _lib.dtype_code(cos2.dtype), half, _lib.ptr(rstd), _lib.ptr(dx), dx.stride(0),
                    _lib.ptr(dw), M, N, _lib.dtype_code(x2.dtype), _lib.dtype_code(weight.dtype),
                    _lib.ptr(ws), ws_bytes, _lib.stream_of(x2))
@@ -56,7 +57,7 @@ class _FusedNormRoPEFunction(torch.autograd.Function):
     """Reference: bloth/bloth/kernels/fused_norm_qkv_rope.py:129-176."""
 
     @staticmethod
-    def forward(ctx, x, weight, cos, sin, eps=1e-6):
+    def forward(ctx, x, weight, cos, sin, eps=1e-6, weight_offset=0.0):
         assert x.is_cuda, "[Bloth] CUDA GPU required"
         _lib.require_cuda(weight, cos, sin)
         orig = x.shape
@@ -66,9 +67,10 @@ class _FusedNormRoPEFunction(torch.autograd.Function):
         M = x2.shape[0]
         cos2 = _lib.aligned16(cos.contiguous().view(M, -1))
         sin2 = _lib.aligned16(sin.contiguous().view(M, -1))
-        y, rstd = norm_rope_forward(x2, weight, cos2, sin2, eps)
+        y, rstd = norm_rope_forward(x2, weight, cos2, sin2, eps, weight_offset)
         ctx.save_for_backward(x2, weight, rstd, cos2, sin2)
         ctx.eps = eps
+        ctx.weight_offset = weight_offset
         ctx.orig = orig
         return y.view(orig)
 
@@ -76,17 +78,19 @@ class _FusedNormRoPEFunction(torch.autograd.Function):
     def backward(ctx, dy):
         x2, weight, rstd, cos2, sin2 = ctx.saved_tensors
         dy2 = _as_rows(dy, x2.shape[1])
-        dx, dw = norm_rope_backward(dy2, x2, weight, cos2, sin2, rstd)
-        return dx.view(ctx.orig), dw, None, None, None
+        dx, dw = norm_rope_backward(dy2, x2, weight, cos2, sin2, rstd, ctx.weight_offset)
+        return dx.view(ctx.orig), dw, None, None, None, None
 
 
 def fused_norm_rope(x: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor,
-                    sin: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+                    sin: torch.Tensor, eps: float = 1e-6,
+                    weight_offset: float = 0.0) -> torch.Tensor:
     """RMSNorm over the last dim of x, then rotate-half RoPE on its first
     2*cos.shape[-1] columns with per-row cos/sin. Same contract as
-    bloth/bloth/kernels/fused_norm_qkv_rope.py:179-203."""
+    bloth/bloth/kernels/fused_norm_qkv_rope.py:179-203; weight_offset (not in
+    the reference) is added to the weight, 1.0 for Gemma-style norms."""
     return _FusedNormRoPEFunction.apply(x, weight.contiguous(), cos.contiguous(),
-                                        sin.contiguous(), eps)
+                                        sin.contiguous(), eps, float(weight_offset))
 
 
 # ------------------------------------------------ per-head q/k (positions)
@@ -155,7 +159,8 @@ def _tables(cos, sin, B: int, S: int, D: int):
 class _QKNormRoPEFunction(torch.autograd.Function):
 
     @staticmethod
-    def forward(ctx, q, k, wq, wk, position_ids, inv_freq, cos, sin, eps):
+    def forward(ctx, q, k, wq, wk, position_ids, inv_freq, cos, sin, eps, weight_offset,
+                rope_scale):
         assert q.is_cuda, "[Bloth] CUDA GPU required"
         _lib.require_cuda(k, wq, wk, position_ids, inv_freq, cos, sin)
         shape_q = q.shape
@@ -184,17 +189,18 @@ class _QKNormRoPEFunction(torch.autograd.Function):
         kpos = None if token_idx else pos
         rc = _lib.call(
             "bloth_qk_norm_rope_fwd", q4, _lib.ptr(q4), _head_strides(q4), _lib.ptr(k4),
-            _head_strides(k4), _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(qo), _head_strides(qo),
-            _lib.ptr(ko), _head_strides(ko), _lib.ptr(rq), _lib.ptr(rk), _lib.ptr(kpos),
-            pos_st if kpos is not None else None,
+            _head_strides(k4), _lib.ptr(wq), _lib.ptr(wk), float(weight_offset), _lib.ptr(qo),
+            _head_strides(qo), _lib.ptr(ko), _head_strides(ko), _lib.ptr(rq), _lib.ptr(rk),
+            _lib.ptr(kpos), pos_st if kpos is not None else None,
             _lib.dtype_code(kpos.dtype) if kpos is not None else 0, _lib.ptr(inv_freq),
             _lib.ptr(cos), _lib.ptr(sin), cs_st, cs_rows,
-            _lib.dtype_code(cos.dtype) if cos is not None else 0, B, S, Hq, Hk, D, float(eps), _lib.dtype_code(q4.dtype), _lib.dtype_code(wq.dtype),
+            _lib.dtype_code(cos.dtype) if cos is not None else 0, float(rope_scale), B, S, Hq,
+            Hk, D, float(eps), _lib.dtype_code(q4.dtype), _lib.dtype_code(wq.dtype),
             _lib.stream_of(q4))
         _lib.check(rc, "qk norm+rope forward")
         ctx.save_for_backward(q4, k4, wq, wk, rq, rk, kpos, inv_freq, cos, sin)
         ctx.meta = (B, S, Hq, Hk, D, pos_st if kpos is not None else None, cs_st, cs_rows,
-                    shape_q, shape_k)
+                    shape_q, shape_k, weight_offset, rope_scale)
         if k4 is None:
             return qo.view(shape_q)
         return qo.view(shape_q), ko.view(shape_k)
@@ -202,7 +208,7 @@ class _QKNormRoPEFunction(torch.autograd.Function):
     @staticmethod
     def backward(ctx, *grads):
         q4, k4, wq, wk, rq, rk, pos, inv_freq, cos, sin = ctx.saved_tensors
-        B, S, Hq, Hk, D, pos_st, cs_st, cs_rows, shape_q, shape_k = ctx.meta
+        B, S, Hq, Hk, D, pos_st, cs_st, cs_rows, shape_q, shape_k, w_off, cs_scale = ctx.meta
         gq = _heads(grads[0].reshape(q4.shape) if grads[0].dim() != 4 else grads[0])
         gk = None
         if k4 is not None:
@@ -218,22 +224,23 @@ class _QKNormRoPEFunction(torch.autograd.Function):
         rc = _lib.call(
             "bloth_qk_norm_rope_bwd", q4, _lib.ptr(gq), _head_strides(gq), _lib.ptr(gk),
             _head_strides(gk), _lib.ptr(q4), _head_strides(q4), _lib.ptr(k4), _head_strides(k4),
-            _lib.ptr(wq), _lib.ptr(wk), _lib.ptr(rq), _lib.ptr(rk), _lib.ptr(dq),
+            _lib.ptr(wq), _lib.ptr(wk), float(w_off), _lib.ptr(rq), _lib.ptr(rk), _lib.ptr(dq),
             _head_strides(dq), _lib.ptr(dk), _head_strides(dk), _lib.ptr(dwq), _lib.ptr(dwk),
             _lib.ptr(pos), pos_st, _lib.dtype_code(pos.dtype) if pos is not None else 0,
             _lib.ptr(inv_freq), _lib.ptr(cos), _lib.ptr(sin), cs_st, cs_rows,
-            _lib.dtype_code(cos.dtype) if cos is not None else 0, B, S, Hq, Hk, D,
-            _lib.dtype_code(q4.dtype), _lib.dtype_code(wq.dtype), _lib.ptr(ws), ws_bytes,
+            _lib.dtype_code(cos.dtype) if cos is not None else 0, float(cs_scale), B, S, Hq, Hk,
+            D, _lib.dtype_code(q4.dtype), _lib.dtype_code(wq.dtype), _lib.ptr(ws), ws_bytes,
             _lib.stream_of(q4))
         _lib.check(rc, "qk norm+rope backward")
         return (dq.view(shape_q), None if dk is None else dk.view(shape_k), dwq, dwk, None, None,
-                None, None, None)
+                None, None, None, None, None)
 
 
 def fused_qk_norm_rope(q: torch.Tensor, k: torch.Tensor | None, wq: torch.Tensor,
                        wk: torch.Tensor | None, position_ids: torch.Tensor | None = None,
                        inv_freq: torch.Tensor | None = None, eps: float = 1e-6,
-                       cos: torch.Tensor | None = None, sin: torch.Tensor | None = None):
+                       cos: torch.Tensor | None = None, sin: torch.Tensor | None = None,
+                       weight_offset: float = 0.0, rope_scale: float = 1.0):
     """Per-head RMSNorm + rotate-half RoPE of q [B, S, Hq, D] and k [B, S, Hk, D].
 
     Each (token, head) row of D is normalised with wq (q) or wk (k) and
@@ -241,7 +248,11 @@ def fused_qk_norm_rope(q: torch.Tensor, k: torch.Tensor | None, wq: torch.Tensor
     (angle = float32(position) * inv_freq, evaluated in-register) or from
     ``cos``/``sin`` tables ([P, D/2|D] indexed by position, or HF's
     [B, S, D] indexed by token). ``position_ids`` [B, S] / [1, S] / [S]
-    default to 0..S-1. Returns (q_out, k_out), or q_out alone when k is None.
-    Shapes and dtypes of the outputs follow the inputs.
+    default to 0..S-1. ``weight_offset`` is added to both weights (1.0 for
+    Gemma-style ``(1 + w)`` norms); ``rope_scale`` multiplies cos and sin (HF's
+    ``attention_scaling``; HF tables already include it, so pass 1.0 with
+    them). Returns (q_out, k_out), or q_out alone when k is None. Shapes and
+    dtypes of the outputs follow the inputs.
     """
-    return _QKNormRoPEFunction.apply(q, k, wq, wk, position_ids, inv_freq, cos, sin, eps)
+    return _QKNormRoPEFunction.apply(q, k, wq, wk, position_ids, inv_freq, cos, sin, eps,
+                                     float(weight_offset), float(rope_scale))

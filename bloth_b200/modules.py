@@ -26,22 +26,30 @@ def rope_inv_freq(head_dim: int, base: float = 10000.0) -> torch.Tensor:
 
 
 class BlothRMSNorm(nn.Module):
-    """Drop-in for LlamaRMSNorm / MistralRMSNorm / Qwen*RMSNorm."""
+    """Drop-in for LlamaRMSNorm / MistralRMSNorm / Qwen*RMSNorm.
 
-    def __init__(self, hidden_size: int, eps: float = 1e-6):
+    ``weight_offset=1.0`` makes it a drop-in for GemmaRMSNorm, whose output is
+    x_hat * (1 + weight) with weight initialised to zeros; the weight is then
+    initialised to 1 - weight_offset so that a fresh module is the identity
+    scale either way."""
+
+    def __init__(self, hidden_size: int, eps: float = 1e-6, weight_offset: float = 0.0):
         super().__init__()
-        self.weight = nn.Parameter(torch.ones(hidden_size))
+        self.weight = nn.Parameter(torch.full((hidden_size,), 1.0 - weight_offset))
         self.eps = eps
+        self.weight_offset = float(weight_offset)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        return _rms_norm_fn(x, self.weight, self.eps)
+        return _rms_norm_fn(x, self.weight, self.eps, self.weight_offset)
 
     def extra_repr(self) -> str:
-        return f"hidden_size={self.weight.shape[0]}, eps={self.eps}"
+        extra = f", weight_offset={self.weight_offset}" if self.weight_offset else ""
+        return f"hidden_size={self.weight.shape[0]}, eps={self.eps}{extra}"
 
 
-def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
-    return _rms_norm_fn(x, weight, eps)
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6,
+             weight_offset: float = 0.0) -> torch.Tensor:
+    return _rms_norm_fn(x, weight, eps, weight_offset)
 
 
 class BlothFusedNormQKV(nn.Module):

@@ -6,6 +6,14 @@ Same entry points and behaviour as the reference's bloth/bloth/patch.py:
 in ``_NORM_CLASS_NAMES`` (:26-43) by a ``BlothRMSNorm`` that shares the
 original ``weight`` Parameter (:46-76), so state_dict keys are unchanged;
 ``FastModel.from_pretrained`` (:133-200) loads a model and patches it.
+
+Two corrections to the reference's norm swap, both silent output changes
+there: Gemma-family norms compute x_hat * (1 + w) (transformers
+GemmaRMSNorm.forward), so they become ``BlothRMSNorm(weight_offset=1.0)``
+rather than an x_hat * w norm; and ``CohereLayerNorm``, although on the
+reference's list, subtracts the mean (it is a LayerNorm), so it is left in
+place. ``patch_attention=True`` (a no-op in the reference) routes supported
+attention modules through the fused kernels (``bloth_b200.attention``).
 """
 from __future__ import annotations
 
@@ -36,6 +44,12 @@ _NORM_CLASS_NAMES = {
     "DeepseekRMSNorm",
 }
 
+# Norms on the list above whose weight enters as (1 + w).
+_WEIGHT_OFFSETS = {"GemmaRMSNorm": 1.0, "Gemma2RMSNorm": 1.0}
+
+# Names on the reference's list that are not RMSNorms and are left in place.
+_NOT_RMS = {"CohereLayerNorm"}
+
 
 def _module_eps(module: nn.Module) -> float:
     """eps lookup order of the reference (patch.py:61-63)."""
@@ -48,13 +62,18 @@ def _replace_norm_layers(model: nn.Module, verbose: bool = True) -> int:
     replaced = 0
     mod_dict = dict(model.named_modules())
     for name, module in list(mod_dict.items()):
-        if type(module).__name__ not in _NORM_CLASS_NAMES:
+        cls = type(module).__name__
+        if cls not in _NORM_CLASS_NAMES or cls in _NOT_RMS:
+            continue
+        weight = getattr(module, "weight", None)
+        if not isinstance(weight, nn.Parameter) or weight.dim() != 1:
             continue
         parts = name.rsplit(".", 1)
         parent = mod_dict[parts[0]] if len(parts) == 2 else model
         attr = parts[-1]
         hidden_size = module.weight.shape[0]
-        norm = BlothRMSNorm(hidden_size, _module_eps(module)).to(
+        norm = BlothRMSNorm(hidden_size, _module_eps(module),
+                            weight_offset=_WEIGHT_OFFSETS.get(cls, 0.0)).to(
             device=module.weight.device, dtype=module.weight.dtype)
         norm.weight = module.weight  # share the Parameter, no copy
         setattr(parent, attr, norm)
@@ -69,8 +88,10 @@ def patch_model(model: nn.Module, patch_norms: bool = True, patch_attention: boo
     """Applies the Bloth kernels to a HuggingFace model in place and returns it.
 
     patch_norms: replace RMSNorm layers (reference behaviour).
-    patch_attention: accepted for signature compatibility; the reference's
-        patcher does nothing with it either (patch.py:79-115).
+    patch_attention: route the q/k normalisation and rotary embedding of
+        supported attention modules through the fused kernels (Qwen3: one
+        fused_qk_norm_rope launch; Llama / Mistral / Qwen2: one RoPE launch
+        for q and k). The reference accepts this flag and does nothing.
     """
     if verbose:
         print(f"\n[Bloth] Patching: {type(model).__name__}")
@@ -80,6 +101,9 @@ def patch_model(model: nn.Module, patch_norms: bool = True, patch_attention: boo
     total = 0
     if patch_norms:
         total += _replace_norm_layers(model, verbose)
+    if patch_attention:
+        from .attention import patch_attention_layers
+        total += patch_attention_layers(model, verbose)
     if total == 0 and verbose:
         warnings.warn("[Bloth] No layers patched. Architecture may not be recognised. "
                       "You can still use bloth_b200.kernels.* directly.")
@@ -94,7 +118,8 @@ class FastModel:
     @staticmethod
     def from_pretrained(model_name: str, max_seq_length: int = 4096, dtype=None,
                         load_in_4bit: bool = False, load_in_8bit: bool = False,
-                        device_map: str = "auto", trust_remote_code: bool = False, **kwargs):
+                        device_map: str = "auto", trust_remote_code: bool = False,
+                        patch_attention: bool = False, **kwargs):
         try:
             from transformers import AutoModelForCausalLM, AutoTokenizer
         except ImportError:
@@ -125,5 +150,5 @@ class FastModel:
         tokenizer = AutoTokenizer.from_pretrained(model_name, trust_remote_code=trust_remote_code)
         if tokenizer.pad_token is None:
             tokenizer.pad_token = tokenizer.eos_token
-        model = patch_model(model, verbose=True)
+        model = patch_model(model, patch_attention=patch_attention, verbose=True)
         return model, tokenizer

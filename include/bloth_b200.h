@@ -14,6 +14,13 @@
  * Head convention (per-head q/k kernels): element [b, s, h, d] of a
  * [B, S, H, D] head tensor is at ptr + b*strides[0] + s*strides[1] +
  * h*strides[2] + d, i.e. the head dimension is contiguous.
+ *
+ * Weight offset: every normalising entry point takes w_offset, a constant
+ * added in fp32 to each weight element before it multiplies the normalised
+ * value: 0 for the usual x_hat * w (Llama, Qwen, Mistral, the reference's
+ * kernels), 1 for the (1 + w) weighting of Gemma-family norms
+ * (transformers GemmaRMSNorm.forward). The weight gradient is the same for
+ * both (d(w + c)/dw = 1).
  */
 #ifndef BLOTH_B200_H_
 #define BLOTH_B200_H_
@@ -71,8 +78,8 @@ int bloth_device_fault(int reset);
  * (bloth/bloth/kernels/rms_norm.py:119-140; kernel :39-73).
  * dtype: type of x and y (F32, BF16, F16); w_dtype: type of w (F32 or dtype).
  * ---------------------------------------------------------------------- */
-int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy,
-                      float* rstd, int64_t M, int64_t N, float eps, int dtype, int w_dtype,
+int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, float w_offset, void* y,
+                      int64_t ldy, float* rstd, int64_t M, int64_t N, float eps, int dtype, int w_dtype,
                       void* stream);
 
 /* Bytes of workspace bloth_rmsnorm_bwd needs for M rows of N on the current
@@ -86,7 +93,7 @@ size_t bloth_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N, int dtype);
    Replaces _RMSNormFunction.backward (bloth/bloth/kernels/rms_norm.py:143-160;
    kernel :76-113). */
 int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
-                      const float* rstd, void* dx, int64_t lddx, void* dw, int64_t M, int64_t N,
+                      float w_offset, const float* rstd, void* dx, int64_t lddx, void* dw, int64_t M, int64_t N,
                       int dtype, int w_dtype, void* workspace, size_t workspace_bytes,
                       void* stream);
 
@@ -106,7 +113,7 @@ int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, 
    capture). All calls share the array, so calls that overlap on the GPU race.
    No counterpart in the reference. */
 int bloth_rmsnorm_bwd_noalloc(const void* dy, int64_t lddy, const void* x, int64_t ldx,
-                              const void* w, const float* rstd, void* dx, int64_t lddx, void* dw,
+                              const void* w, float w_offset, const float* rstd, void* dx, int64_t lddx, void* dw,
                               int64_t M, int64_t N, int dtype, int w_dtype, void* stream);
 
 /* ------------------------------------------------------------------------
@@ -119,7 +126,7 @@ int bloth_rmsnorm_bwd_noalloc(const void* dy, int64_t lddy, const void* x, int64
  * Replaces _FusedNormRoPEFunction.forward
  * (bloth/bloth/kernels/fused_norm_qkv_rope.py:132-159; kernel :40-96).
  * ---------------------------------------------------------------------- */
-int bloth_norm_rope_fwd(const void* x, int64_t ldx, const void* w, const void* cos,
+int bloth_norm_rope_fwd(const void* x, int64_t ldx, const void* w, float w_offset, const void* cos,
                         const void* sin, int64_t ldcs, int cs_dtype, int64_t half, void* y,
                         int64_t ldy, float* rstd, int64_t M, int64_t N, float eps, int dtype,
                         int w_dtype, void* stream);
@@ -132,7 +139,7 @@ size_t bloth_norm_rope_bwd_workspace_bytes(int64_t M, int64_t N, int dtype);
    (bloth/bloth/kernels/fused_norm_qkv_rope.py:99-126) omits the rotation.
    Replaces _FusedNormRoPEFunction.backward (:161-176). */
 int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
-                        const void* cos, const void* sin, int64_t ldcs, int cs_dtype,
+                        float w_offset, const void* cos, const void* sin, int64_t ldcs, int cs_dtype,
                         int64_t half, const float* rstd, void* dx, int64_t lddx, void* dw,
                         int64_t M, int64_t N, int dtype, int w_dtype, void* workspace,
                         size_t workspace_bytes, void* stream);
@@ -148,6 +155,8 @@ int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx
  *     p = pos[b, s] (or s when pos is NULL) clamped to [0, cs_rows - 1];
  *     elements [0, D/2) of the row are used, so full-width [.., D] tables
  *     with duplicated halves also work.
+ * rope_scale multiplies cos and sin from either source (HF's
+ *   attention_scaling of YaRN / LongRoPE rotary embeddings; 1 otherwise).
  * pos: [B, S] positions (I64 or I32) at pos + b*pos_strides[0] +
  *   s*pos_strides[1]; NULL means pos = s. Packed sequences pass positions that
  *   restart at each document.
@@ -160,12 +169,13 @@ int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx
  * apply_rotary_pos_emb pair that patch_model leaves in place (patch.py:46-76).
  * ---------------------------------------------------------------------- */
 int bloth_qk_norm_rope_fwd(const void* q, const int64_t* q_strides, const void* k,
-                           const int64_t* k_strides, const void* wq, const void* wk, void* q_out,
-                           const int64_t* qo_strides, void* k_out, const int64_t* ko_strides,
-                           float* rstd_q, float* rstd_k, const void* pos,
-                           const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
-                           const void* cos, const void* sin, const int64_t* cs_strides,
-                           int64_t cs_rows, int cs_dtype, int64_t B, int64_t S, int64_t Hq,
+                           const int64_t* k_strides, const void* wq, const void* wk,
+                           float w_offset, void* q_out, const int64_t* qo_strides, void* k_out,
+                           const int64_t* ko_strides, float* rstd_q, float* rstd_k,
+                           const void* pos, const int64_t* pos_strides, int pos_dtype,
+                           const float* inv_freq, const void* cos, const void* sin,
+                           const int64_t* cs_strides, int64_t cs_rows, int cs_dtype,
+                           float rope_scale, int64_t B, int64_t S, int64_t Hq,
                            int64_t Hk, int64_t D, float eps, int dtype, int w_dtype, void* stream);
 
 size_t bloth_qk_norm_rope_bwd_workspace_bytes(int64_t B, int64_t S, int64_t D, int dtype);
@@ -176,29 +186,35 @@ size_t bloth_qk_norm_rope_bwd_workspace_bytes(int64_t B, int64_t S, int64_t D, i
 int bloth_qk_norm_rope_bwd(const void* dq_out, const int64_t* dqo_strides, const void* dk_out,
                            const int64_t* dko_strides, const void* q, const int64_t* q_strides,
                            const void* k, const int64_t* k_strides, const void* wq,
-                           const void* wk, const float* rstd_q, const float* rstd_k, void* dq,
+                           const void* wk, float w_offset, const float* rstd_q,
+                           const float* rstd_k, void* dq,
                            const int64_t* dq_strides, void* dk, const int64_t* dk_strides,
                            void* dwq, void* dwk, const void* pos, const int64_t* pos_strides,
                            int pos_dtype, const float* inv_freq, const void* cos,
                            const void* sin, const int64_t* cs_strides, int64_t cs_rows,
-                           int cs_dtype, int64_t B, int64_t S, int64_t Hq, int64_t Hk, int64_t D,
+                           int cs_dtype, float rope_scale, int64_t B, int64_t S, int64_t Hq,
+                           int64_t Hk, int64_t D,
                            int dtype, int w_dtype, void* workspace, size_t workspace_bytes,
                            void* stream);
 
 /* ------------------------------------------------------------------------
- * Rotate-half RoPE alone over a [B, S, H, D] head tensor (same cos/sin and
- * position rules as above). transpose = 0 applies the rotation
- * (y1 = x1*cos - x2*sin, y2 = x1*sin + x2*cos); transpose = 1 applies its
- * transpose, which is the backward (dx from dy).
+ * Rotate-half RoPE alone over q [B, S, Hq, D] and k [B, S, Hk, D] head
+ * tensors in one launch (same cos/sin, position and rope_scale rules as
+ * above; k, k_out may be NULL when Hk == 0). transpose = 0 applies the
+ * rotation (y1 = x1*cos - x2*sin, y2 = x1*sin + x2*cos); transpose = 1
+ * applies its transpose, which is the backward (dx from dy).
  * Replaces rope_embedding / _rope_kernel (bloth/bloth/ops/rope.py:9-58), which
- * is forward-only and always stores bf16; here the output has x's type.
+ * is forward-only, rotates one tensor and always stores bf16; here the
+ * outputs have the inputs' type. With q and k it also replaces HF's
+ * apply_rotary_pos_emb(q, k, cos, sin) for RoPE-only attention (Llama,
+ * Mistral, Qwen2).
  * ---------------------------------------------------------------------- */
-int bloth_rope(const void* x, const int64_t* x_strides, void* y, const int64_t* y_strides,
+int bloth_rope(const void* q, const int64_t* q_strides, void* q_out, const int64_t* qo_strides,
+               const void* k, const int64_t* k_strides, void* k_out, const int64_t* ko_strides,
                const void* pos, const int64_t* pos_strides, int pos_dtype, const float* inv_freq,
                const void* cos, const void* sin, const int64_t* cs_strides, int64_t cs_rows,
-               int cs_dtype, int64_t B, int64_t S, int64_t H, int64_t D, int transpose, int dtype,
-               void* stream);
-
+               int cs_dtype, float rope_scale, int64_t B, int64_t S, int64_t Hq, int64_t Hk,
+               int64_t D, int transpose, int dtype, void* stream);
 #ifdef __cplusplus
 }
 #endif

@@ -25,6 +25,18 @@ Reference semantics restated (paths relative to the reference project):
   ``compute`` precision.
 * RoPE alone: bloth/bloth/ops/rope.py:21-27 (same rotation, no norm).
 
+Two extensions the reference does not have, restated from the third-party
+code they serve (transformers 5.5.0 as installed):
+
+* ``w_offset``: the weight enters as ``w + w_offset``; 1.0 is GemmaRMSNorm's
+  ``_norm(x.float()) * (1.0 + weight.float())`` (models/gemma/
+  modeling_gemma.py, GemmaRMSNorm.forward). The reference's patcher puts an
+  ``x_hat * w`` norm in place of GemmaRMSNorm (bloth/bloth/patch.py:33-34,
+  :46-76), which is not this function.
+* ``rope_scale``: cos and sin multiplied by the rotary embedding's
+  ``attention_scaling`` (models/llama/modeling_llama.py,
+  LlamaRotaryEmbedding.forward: ``cos = emb.cos() * self.attention_scaling``).
+
 The reference's fused backward kernel (fused_norm_qkv_rope.py:99-126) is a
 plain RMSNorm backward that never applies the transposed rotation, so it is
 not the gradient of its forward. ``norm_rope_table_reference_bwd`` restates
@@ -76,13 +88,14 @@ def _rotate(n: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, half: int):
 
 
 # ------------------------------------------------------------------ RMSNorm
-def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, compute=F64):
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, compute=F64,
+             w_offset: float = 0.0):
     """(y in x.dtype, rstd float32) - bloth/tests/test_kernels.py:124-127."""
-    y, rstd = _rms_core(x.to(compute), w.to(compute), eps)
+    y, rstd = _rms_core(x.to(compute), w.to(compute) + w_offset, eps)
     return y.to(x.dtype), rstd.to(torch.float32)
 
 
-def rms_norm_fwd_bwd(x, w, dy, eps: float = 1e-6, compute=F64):
+def rms_norm_fwd_bwd(x, w, dy, eps: float = 1e-6, compute=F64, w_offset: float = 0.0):
     """Forward plus the autograd backward of :func:`rms_norm`.
 
     Returns y, rstd, dx (x.dtype), dw (w.dtype). The gradient equals the
@@ -90,7 +103,7 @@ def rms_norm_fwd_bwd(x, w, dy, eps: float = 1e-6, compute=F64):
     """
     xc = x.detach().to(compute).requires_grad_(True)
     wc = w.detach().to(compute).requires_grad_(True)
-    y, rstd = _rms_core(xc, wc, eps)
+    y, rstd = _rms_core(xc, wc + w_offset, eps)
     y.backward(dy.to(compute))
     return (y.detach().to(x.dtype), rstd.detach().to(torch.float32),
             xc.grad.to(x.dtype), wc.grad.to(w.dtype))
@@ -137,15 +150,17 @@ def norm_rope_table_reference_bwd(x, w, rstd, dy, compute=F64):
 
 
 # ------------------------------------- per-head q/k norm + RoPE (positions)
-def _head_cos_sin(pos, inv_f, cos_tab, sin_tab, compute, D):
-    """cos/sin [B, S, 1, D/2] from positions and inv_freq, or from tables."""
+def _head_cos_sin(pos, inv_f, cos_tab, sin_tab, compute, D, scale: float = 1.0):
+    """cos/sin [B, S, 1, D/2] from positions and inv_freq, or from tables,
+    multiplied by ``scale``."""
     if cos_tab is not None:
         c, s = cos_tab[..., : D // 2], sin_tab[..., : D // 2]
         if c.dim() == 2:  # [P, D/2] indexed by position
             c, s = c[pos], s[pos]
-        return c.to(compute).unsqueeze(-2), s.to(compute).unsqueeze(-2)
-    c, s = rope_cos_sin(pos, inv_f, compute)
-    return c.unsqueeze(-2), s.unsqueeze(-2)
+        c, s = c.to(compute), s.to(compute)
+    else:
+        c, s = rope_cos_sin(pos, inv_f, compute)
+    return (c * scale).unsqueeze(-2), (s * scale).unsqueeze(-2)
 
 
 def _positions(B: int, S: int, position_ids, device=None):
@@ -158,7 +173,8 @@ def _positions(B: int, S: int, position_ids, device=None):
 
 
 def qk_norm_rope(q, k, wq, wk, position_ids=None, inv_f=None, eps: float = 1e-6,
-                 cos=None, sin=None, compute=F64):
+                 cos=None, sin=None, compute=F64, w_offset: float = 0.0,
+                 rope_scale: float = 1.0):
     """Per-head RMSNorm then rotate-half RoPE for q [B,S,Hq,D] and k [B,S,Hk,D].
 
     Per (token, head) row this is exactly :func:`norm_rope_table` with
@@ -168,33 +184,34 @@ def qk_norm_rope(q, k, wq, wk, position_ids=None, inv_f=None, eps: float = 1e-6,
     """
     B, S, _, D = q.shape
     pos = _positions(B, S, position_ids, q.device)
-    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
+    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D, rope_scale)
     outs = []
     for x, w in ((q, wq), (k, wk)):
         if x is None:
             outs.append((None, None))
             continue
-        n, rstd = _rms_core(x.to(compute), w.to(compute), eps)
+        n, rstd = _rms_core(x.to(compute), w.to(compute) + w_offset, eps)
         outs.append((_rotate(n, c, s, D // 2).to(x.dtype), rstd.to(torch.float32)))
     return outs[0][0], outs[1][0], outs[0][1], outs[1][1]
 
 
 def qk_norm_rope_fwd_bwd(q, k, wq, wk, dq_out, dk_out, position_ids=None, inv_f=None,
-                         eps: float = 1e-6, cos=None, sin=None, compute=F64):
+                         eps: float = 1e-6, cos=None, sin=None, compute=F64,
+                         w_offset: float = 0.0, rope_scale: float = 1.0):
     """Forward and exact backward of :func:`qk_norm_rope`.
 
     Returns dict with q_out, k_out, rstd_q, rstd_k, dq, dk, dwq, dwk.
     """
     B, S, _, D = q.shape
     pos = _positions(B, S, position_ids, q.device)
-    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
+    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D, rope_scale)
     res = {}
     for name, x, w, g in (("q", q, wq, dq_out), ("k", k, wk, dk_out)):
         if x is None:
             continue
         xc = x.detach().to(compute).requires_grad_(True)
         wc = w.detach().to(compute).requires_grad_(True)
-        n, rstd = _rms_core(xc, wc, eps)
+        n, rstd = _rms_core(xc, wc + w_offset, eps)
         y = _rotate(n, c, s, D // 2)
         y.backward(g.to(compute))
         res[name + "_out"] = y.detach().to(x.dtype)
@@ -206,20 +223,21 @@ def qk_norm_rope_fwd_bwd(q, k, wq, wk, dq_out, dk_out, position_ids=None, inv_f=
 
 # ----------------------------------------------------------------- RoPE only
 def rope(x, position_ids=None, inv_f=None, cos=None, sin=None, compute=F64,
-         out_dtype=None):
+         out_dtype=None, rope_scale: float = 1.0):
     """Rotate-half RoPE of x [B, S, H, D] - bloth/bloth/ops/rope.py:21-27."""
     B, S, _, D = x.shape
     pos = _positions(B, S, position_ids, x.device)
-    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
+    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D, rope_scale)
     y = _rotate(x.to(compute), c, s, D // 2)
     return y.to(out_dtype or x.dtype)
 
 
-def rope_fwd_bwd(x, dy, position_ids=None, inv_f=None, cos=None, sin=None, compute=F64):
+def rope_fwd_bwd(x, dy, position_ids=None, inv_f=None, cos=None, sin=None, compute=F64,
+                 rope_scale: float = 1.0):
     """RoPE forward and its exact backward (the transposed rotation)."""
     B, S, _, D = x.shape
     pos = _positions(B, S, position_ids, x.device)
-    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D)
+    c, s = _head_cos_sin(pos, inv_f, cos, sin, compute, D, rope_scale)
     xc = x.detach().to(compute).requires_grad_(True)
     y = _rotate(xc, c, s, D // 2)
     y.backward(dy.to(compute))

@@ -1,6 +1,7 @@
 """The C-ABI library loads without a GPU and exports every declared entry
 point; host-side argument handling raises the reference's errors. CPU only:
 no kernel is launched here."""
+import ctypes
 import os
 import re
 
@@ -20,10 +21,54 @@ def declared_symbols():
     return sorted(set(re.findall(r"\b(bloth_\w+)\s*\(", text)))
 
 
+def declared_prototypes():
+    """{name: (return type, [argument types])} of every prototype in the header,
+    types as written in C with the parameter names removed."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = "\n".join(ln for ln in text.splitlines() if not ln.lstrip().startswith("#"))
+    out = {}
+    for ret, name, args in re.findall(r"([\w\s\*]+?)\s*\b(bloth_\w+)\s*\(([^)]*)\)\s*;", text):
+        types = []
+        for arg in args.split(","):
+            arg = " ".join(arg.split())
+            if arg in ("", "void"):
+                continue
+            m = re.match(r"(.*?[\s\*])(\w+)$", arg)
+            types.append(m.group(1).replace(" ", "").replace("const", "const "))
+        out[name] = (" ".join(ret.split()), types)
+    return out
+
+
+_CTYPES_OF = {
+    "int": ctypes.c_int, "int64_t": ctypes.c_int64, "float": ctypes.c_float,
+    "size_t": ctypes.c_size_t, "const char*": ctypes.c_char_p,
+    "const int64_t*": ctypes.POINTER(ctypes.c_int64),
+}
+
+
+def ctypes_of(ctype: str):
+    if ctype in _CTYPES_OF:
+        return _CTYPES_OF[ctype]
+    assert ctype.endswith("*"), ctype
+    return ctypes.c_void_p  # data pointers and cudaStream_t
+
+
 def test_library_built_and_loads():
     assert os.path.exists(_lib.LIB_PATH), "run python -m bloth_b200.build"
     lib = _lib.load()
-    assert lib.bloth_version() == (0 << 16) | (1 << 8) | 0
+    assert lib.bloth_version() == (0 << 16) | (2 << 8) | 0
+
+
+def test_ctypes_signatures_match_the_header():
+    protos = declared_prototypes()
+    assert sorted(protos) == declared_symbols()
+    for name, (ret, args) in protos.items():
+        res, argtypes = _lib._SIGNATURES[name]
+        assert res is ctypes_of(ret.replace(" *", "*")), name
+        assert len(argtypes) == len(args), (name, len(argtypes), len(args))
+        for i, (got, want) in enumerate(zip(argtypes, args)):
+            assert got is ctypes_of(want), (name, i, want)
 
 
 def test_every_declared_symbol_is_exported_and_bound():
@@ -45,23 +90,27 @@ def test_strerror_texts():
 def test_validation_errors_without_gpu():
     # argument checks run before any CUDA call, so they answer on a CPU host
     lib = _lib.load()
-    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 1, 70000, 1e-6, 1, 1, None) == 2
-    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 1, 40000, 1e-6, 0, 0, None) == 2
-    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 1, 64, 1e-6, 7, 1, None) == 1
-    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 4, 64, 1e-6, 1, 1, None) == 5
+    fwd = lib.bloth_rmsnorm_fwd
+    assert fwd(None, 0, None, 0.0, None, 0, None, 1, 70000, 1e-6, 1, 1, None) == 2
+    assert fwd(None, 0, None, 0.0, None, 0, None, 1, 40000, 1e-6, 0, 0, None) == 2
+    assert fwd(None, 0, None, 0.0, None, 0, None, 1, 64, 1e-6, 7, 1, None) == 1
+    assert fwd(None, 0, None, 1.0, None, 0, None, 4, 64, 1e-6, 1, 1, None) == 5
     # M == 0 is a no-op
-    assert lib.bloth_rmsnorm_fwd(None, 0, None, None, 0, None, 0, 64, 1e-6, 1, 1, None) == 0
+    assert fwd(None, 0, None, 0.0, None, 0, None, 0, 64, 1e-6, 1, 1, None) == 0
     # rotated part wider than the row
-    assert lib.bloth_norm_rope_fwd(None, 0, None, None, None, 0, 0, 40, None, 0, None, 4, 64,
-                                   1e-6, 1, 1, None) == 2
+    assert lib.bloth_norm_rope_fwd(None, 0, None, 0.0, None, None, 0, 0, 40, None, 0, None, 4,
+                                   64, 1e-6, 1, 1, None) == 2
     # head_dim outside {64, 128, 256}
     st = _lib.strides((0, 0, 0))
-    assert lib.bloth_rope(None, st, None, st, None, None, 0, None, None, None, None, 0, 0, 1, 1,
-                          1, 96, 0, 1, None) == 2
+    assert lib.bloth_rope(None, st, None, st, None, None, None, None, None, None, 0, None, None,
+                          None, None, 0, 0, 1.0, 1, 1, 1, 0, 96, 0, 1, None) == 2
+    # no heads at all
+    assert lib.bloth_rope(None, st, None, st, None, None, None, None, None, None, 0, None, None,
+                          None, None, 0, 0, 1.0, 1, 1, 0, 0, 64, 0, 1, None) == 2
     # both a table and inv_freq
     dummy = _lib.ptr(torch.zeros(1))
-    assert lib.bloth_rope(None, st, None, st, None, None, 0, dummy, dummy, dummy, st, 1, 0, 1, 1,
-                          1, 64, 0, 1, None) == 7
+    assert lib.bloth_rope(None, st, None, st, None, None, None, None, None, None, 0, dummy, dummy,
+                          dummy, st, 1, 0, 1.0, 1, 1, 1, 0, 64, 0, 1, None) == 7
 
 
 def test_cpu_tensors_raise_like_the_reference():

@@ -370,6 +370,20 @@ def test_rmsnorm_edge_shapes(cuda):
                torch.bfloat16, "strided rows")
 
 
+def test_rmsnorm_row_widths_sharing_a_kernel_in_any_order(cuda):
+    # fp32 rows of 1024 and of 520 run the same pipelined kernel with different
+    # shared-memory sizes; a wide call after a narrow one must still launch
+    for N in (1024, 520, 1024, 700, 1024):
+        x = seeded_normal((300, N), torch.float32, N).to(cuda)
+        w = seeded_weight(N, torch.float32, 1).to(cuda)
+        g = seeded_normal((300, N), torch.float32, 2).to(cuda)
+        y, dx, dw = run_rms(x, w, g, 1e-6)
+        ry, _, rdx, rdw = oracle.rms_norm_fwd_bwd(x.cpu(), w.cpu(), g.cpu(), 1e-6)
+        assert_tol(y.cpu(), ry, torch.float32, f"y N={N}")
+        assert_tol(dx.cpu(), rdx, torch.float32, f"dx N={N}")
+        assert_tol(dw.cpu(), rdw, torch.float32, f"dw N={N}", True)
+
+
 def test_rmsnorm_empty_and_determinism(cuda):
     x = torch.empty(0, 256, device=cuda, dtype=torch.bfloat16, requires_grad=True)
     w = torch.ones(256, device=cuda, dtype=torch.bfloat16, requires_grad=True)

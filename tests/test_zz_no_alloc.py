@@ -31,14 +31,14 @@ def _backward(dy, x, w, rstd, noalloc: bool):
     code, wcode = _lib.dtype_code(x.dtype), _lib.dtype_code(w.dtype)
     stream = _lib.stream_of(x)
     if noalloc:
-        rc = lib.bloth_rmsnorm_bwd_noalloc(_lib.ptr(dy), N, _lib.ptr(x), N, _lib.ptr(w),
+        rc = lib.bloth_rmsnorm_bwd_noalloc(_lib.ptr(dy), N, _lib.ptr(x), N, _lib.ptr(w), 0.0,
                                            _lib.ptr(rstd), _lib.ptr(dx), N, _lib.ptr(dw), M, N,
                                            code, wcode, stream)
     else:
         ws_bytes = lib.bloth_rmsnorm_bwd_workspace_bytes(M, N, code)
         ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=x.device)
-        rc = lib.bloth_rmsnorm_bwd(_lib.ptr(dy), N, _lib.ptr(x), N, _lib.ptr(w), _lib.ptr(rstd),
-                                   _lib.ptr(dx), N, _lib.ptr(dw), M, N, code, wcode,
+        rc = lib.bloth_rmsnorm_bwd(_lib.ptr(dy), N, _lib.ptr(x), N, _lib.ptr(w), 0.0,
+                                   _lib.ptr(rstd), _lib.ptr(dx), N, _lib.ptr(dw), M, N, code, wcode,
                                    _lib.ptr(ws), ws_bytes, stream)
     torch.cuda.synchronize()
     assert rc == 0, lib.bloth_strerror(rc)
@@ -73,7 +73,7 @@ def test_noalloc_rejects_calls_beyond_the_scratch(cuda):
     assert need > SCRATCH
     # rejected during argument checks, before any kernel is launched
     one = torch.zeros(16, dtype=torch.bfloat16, device=cuda)
-    rc = lib.bloth_rmsnorm_bwd_noalloc(_lib.ptr(one), N, _lib.ptr(one), N, _lib.ptr(one),
+    rc = lib.bloth_rmsnorm_bwd_noalloc(_lib.ptr(one), N, _lib.ptr(one), N, _lib.ptr(one), 0.0,
                                        _lib.ptr(one), _lib.ptr(one), N, _lib.ptr(one), M, N,
                                        _lib.BF16, _lib.BF16, _lib.stream_of(one))
     assert rc == 4  # BLOTH_ERR_WORKSPACE
