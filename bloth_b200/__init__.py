@@ -10,8 +10,9 @@ and kernels/__init__.py:7-8):
 plus fused_qk_norm_rope / BlothQKNormRoPE (q and k per-head norm + RoPE in one
 launch, cos/sin from positions in-register or from HF tables), apply_rope_qk /
 apply_rotary_pos_emb (RoPE of q and k in one launch), the (1 + w) weighting of
-Gemma-family norms (weight_offset), and patch_model(..., patch_attention=True),
-which routes HF Qwen3 / Llama / Mistral / Qwen2 attention through them. The compute runs in hand-written
+Gemma-family norms (weight_offset), fused_add_rms_norm (residual add + RMSNorm
+in one pass), and patch_model(..., patch_attention=True, patch_residual=True),
+which routes HF Qwen3 / Llama / Mistral / Qwen2 layers through them. The compute runs in hand-written
 CUDA behind the C ABI of include/bloth_b200.h; importing this package does not
 touch the GPU, and every op raises if the library or a CUDA device is missing.
 """
@@ -24,6 +25,7 @@ from .kernels import (  # noqa: F401
     apply_rope,
     apply_rope_qk,
     apply_rotary_pos_emb,
+    fused_add_rms_norm,
     fused_norm_rope,
     fused_qk_norm_rope,
 )
@@ -45,6 +47,7 @@ __all__ = [
     "BlothRMSNorm",
     "fused_norm_qkv",
     "BlothFusedNormQKV",
+    "fused_add_rms_norm",
     "fused_norm_rope",
     "fused_qk_norm_rope",
     "BlothQKNormRoPE",

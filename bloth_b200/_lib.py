@@ -50,6 +50,11 @@ _SIGNATURES = {
                                  _int, _int, _vp, _sz, _vp]),
     "bloth_rmsnorm_bwd_noalloc": (_int, [_vp, _i64, _vp, _i64, _vp, _f32, _vp, _vp, _i64, _vp,
                                          _i64, _i64, _int, _int, _vp]),
+    "bloth_add_rmsnorm_fwd": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _f32, _vp, _i64, _vp,
+                                     _i64, _i64, _f32, _int, _int, _vp]),
+    "bloth_add_rmsnorm_bwd_workspace_bytes": (_sz, [_i64, _i64, _int]),
+    "bloth_add_rmsnorm_bwd": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _vp, _f32, _vp, _vp, _i64,
+                                     _vp, _i64, _i64, _int, _int, _vp, _sz, _vp]),
     "bloth_norm_rope_fwd": (_int, [_vp, _i64, _vp, _f32, _vp, _vp, _i64, _int, _i64, _vp, _i64,
                                    _vp, _i64, _i64, _f32, _int, _int, _vp]),
     "bloth_norm_rope_bwd_workspace_bytes": (_sz, [_i64, _i64, _int]),

@@ -1,4 +1,5 @@
-"""HuggingFace attention binding: ``patch_model(..., patch_attention=True)``.
+"""HuggingFace layer bindings: ``patch_model(..., patch_attention=True,
+patch_residual=True)``.
 
 The reference accepts ``patch_attention`` but does nothing with it
 (bloth/bloth/patch.py:79-115; its model_patcher.py attention path cannot be
@@ -21,6 +22,13 @@ another signature, whose head_dim the kernels do not take (64, 128, 256) or
 whose q and k norms differ in eps or weighting is left unpatched and reported.
 The binding is per module instance; other models of the same class in the
 process are untouched.
+
+``patch_residual=True`` binds, per decoder layer (``LlamaDecoderLayer``,
+``MistralDecoderLayer``, ``Qwen2DecoderLayer``, ``Qwen3DecoderLayer``), a
+forward in which the attention block's residual add and the
+``post_attention_layernorm`` that follows it are one ``fused_add_rms_norm``
+launch (transformers models/llama/modeling_llama.py,
+LlamaDecoderLayer.forward); the rest of the layer is HF's code.
 """
 from __future__ import annotations
 
@@ -32,6 +40,7 @@ from dataclasses import dataclass
 
 import torch.nn as nn
 
+from .kernels.add_rms_norm import fused_add_rms_norm
 from .kernels.fused_norm_qkv_rope import fused_qk_norm_rope
 from .kernels.rope import apply_rope_qk
 from .modules import BlothRMSNorm
@@ -148,4 +157,52 @@ def patch_attention_layers(model: nn.Module, verbose: bool = True) -> int:
                       (f" (+{len(skipped) - 4} more)" if len(skipped) > 4 else ""))
     if verbose and bound > 0:
         print(f"[Bloth] Patched {bound} attention layer(s) -> fused q/k norm + RoPE")
+    return bound
+
+
+# ------------------------------------------------- decoder layer: residual add
+_DECODER_CLASSES = {"LlamaDecoderLayer", "MistralDecoderLayer", "Qwen2DecoderLayer",
+                    "Qwen3DecoderLayer"}
+_DECODER_PARAMS = ["self", "hidden_states", "attention_mask", "position_ids", "past_key_values",
+                   "use_cache", "position_embeddings", "kwargs"]
+
+
+def _decoder_layer_forward(self, hidden_states, attention_mask=None, position_ids=None,
+                           past_key_values=None, use_cache=False, position_embeddings=None,
+                           **kwargs):
+    """HF 5.x decoder layer with residual add + post-attention norm fused."""
+    residual = hidden_states
+    hidden_states = self.input_layernorm(hidden_states)
+    hidden_states, _ = self.self_attn(
+        hidden_states=hidden_states, attention_mask=attention_mask, position_ids=position_ids,
+        past_key_values=past_key_values, use_cache=use_cache,
+        position_embeddings=position_embeddings, **kwargs)
+    w, eps, off = _norm_params(self.post_attention_layernorm)
+    hidden_states, residual = fused_add_rms_norm(hidden_states, residual, w, eps, off)
+    hidden_states = self.mlp(hidden_states)
+    return residual + hidden_states
+
+
+def patch_decoder_layers(model: nn.Module, verbose: bool = True) -> int:
+    """Binds the fused residual forward to every supported decoder layer;
+    returns how many were bound."""
+    bound, skipped = 0, []
+    for name, module in model.named_modules():
+        if type(module).__name__ not in _DECODER_CLASSES or "forward" in module.__dict__:
+            continue
+        params = list(inspect.signature(type(module).forward).parameters)
+        if params != _DECODER_PARAMS:
+            skipped.append(f"{name}: forward{tuple(params[1:])} is not the transformers 5.x "
+                           "signature")
+            continue
+        if _norm_params(getattr(module, "post_attention_layernorm", None)) is None:
+            skipped.append(f"{name}: post_attention_layernorm is not a recognised RMSNorm")
+            continue
+        module.forward = types.MethodType(_decoder_layer_forward, module)
+        bound += 1
+    if skipped:
+        warnings.warn("[Bloth] decoder layers left unpatched - " + "; ".join(skipped[:4]) +
+                      (f" (+{len(skipped) - 4} more)" if len(skipped) > 4 else ""))
+    if verbose and bound > 0:
+        print(f"[Bloth] Patched {bound} decoder layer(s) -> fused residual add + RMSNorm")
     return bound

@@ -185,7 +185,7 @@ int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, float w_offset,
   a.ldo = ldy;
   a.rstd_out = rstd;
   return dispatch_dtype(dtype, [&](auto t) {
-    return rows_fwd<decltype(t)>(a, false, vec, as_stream(stream));
+    return rows_fwd<decltype(t)>(a, kRowNorm, vec, as_stream(stream));
   });
 }
 
@@ -193,7 +193,7 @@ size_t bloth_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N, int dtype) {
   if (check_rows(M, N, dtype, dtype)) return 0;
   size_t bytes = 0;
   dispatch_dtype(dtype, [&](auto t) {
-    bytes = rows_bwd_workspace<decltype(t)>(M, (int)N, false);
+    bytes = rows_bwd_workspace<decltype(t)>(M, (int)N, kRowNorm);
     return 0;
   });
   return bytes;
@@ -219,7 +219,8 @@ int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, 
   a.ldo = lddx;
   a.rstd_in = rstd;
   return dispatch_dtype(dtype, [&](auto t) {
-    return rows_bwd<decltype(t)>(a, false, vec, workspace, workspace_bytes, dw, as_stream(stream));
+    return rows_bwd<decltype(t)>(a, kRowNorm, vec, workspace, workspace_bytes, dw,
+                                 as_stream(stream));
   });
 }
 
@@ -250,7 +251,7 @@ int bloth_norm_rope_fwd(const void* x, int64_t ldx, const void* w, float w_offse
   const int vecw = 16 / elem_size(dtype);
   a.cs_vec = aligned(cos, 16) && aligned(sin, 16) && ldcs % vecw == 0;
   return dispatch_dtype(dtype, [&](auto t) {
-    return rows_fwd<decltype(t)>(a, true, vec, as_stream(stream));
+    return rows_fwd<decltype(t)>(a, kRowRope, vec, as_stream(stream));
   });
 }
 
@@ -258,7 +259,7 @@ size_t bloth_norm_rope_bwd_workspace_bytes(int64_t M, int64_t N, int dtype) {
   if (check_rows(M, N, dtype, dtype)) return 0;
   size_t bytes = 0;
   dispatch_dtype(dtype, [&](auto t) {
-    bytes = rows_bwd_workspace<decltype(t)>(M, (int)N, true);
+    bytes = rows_bwd_workspace<decltype(t)>(M, (int)N, kRowRope);
     return 0;
   });
   return bytes;
@@ -293,7 +294,75 @@ int bloth_norm_rope_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx
   const int vecw = 16 / elem_size(dtype);
   a.cs_vec = aligned(cos, 16) && aligned(sin, 16) && ldcs % vecw == 0;
   return dispatch_dtype(dtype, [&](auto t) {
-    return rows_bwd<decltype(t)>(a, true, vec, workspace, workspace_bytes, dw, as_stream(stream));
+    return rows_bwd<decltype(t)>(a, kRowRope, vec, workspace, workspace_bytes, dw,
+                                 as_stream(stream));
+  });
+}
+
+// ------------------------------------------------ residual add + RMSNorm
+int bloth_add_rmsnorm_fwd(const void* x, int64_t ldx, const void* r, int64_t ldr, void* z,
+                          int64_t ldz, const void* w, float w_offset, void* y, int64_t ldy,
+                          float* rstd, int64_t M, int64_t N, float eps, int dtype, int w_dtype,
+                          void* stream) {
+  int rc = check_rows(M, N, dtype, w_dtype);
+  if (rc) return rc;
+  if (M == 0) return BLOTH_OK;
+  if (!x || !r || !z || !w || !y || !rstd) return BLOTH_ERR_NULL;
+  if ((rc = check_ld(M, N, {ldx, ldr, ldz, ldy}))) return rc;
+  const bool vec = rows_vec_ok(dtype, N, {x, r, z, y}, {ldx, ldr, ldz, ldy});
+  if (!vec && N > kMaxScalarRow) return BLOTH_ERR_ALIGN;
+  RowArgs a = make_rows(M, N, eps, w, w_offset, w_dtype);
+  a.x = x;
+  a.ldx = ldx;
+  a.res = r;
+  a.ldres = ldr;
+  a.res_out = z;
+  a.ldres_out = ldz;
+  a.out = y;
+  a.ldo = ldy;
+  a.rstd_out = rstd;
+  return dispatch_dtype(dtype, [&](auto t) {
+    return rows_fwd<decltype(t)>(a, kRowAdd, vec, as_stream(stream));
+  });
+}
+
+size_t bloth_add_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N, int dtype) {
+  if (check_rows(M, N, dtype, dtype)) return 0;
+  size_t bytes = 0;
+  dispatch_dtype(dtype, [&](auto t) {
+    bytes = rows_bwd_workspace<decltype(t)>(M, (int)N, kRowAdd);
+    return 0;
+  });
+  return bytes;
+}
+
+int bloth_add_rmsnorm_bwd(const void* dy, int64_t lddy, const void* dz_out, int64_t lddz_out,
+                          const void* z, int64_t ldz, const void* w, float w_offset,
+                          const float* rstd, void* dz, int64_t lddz, void* dw, int64_t M,
+                          int64_t N, int dtype, int w_dtype, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  int rc = check_rows(M, N, dtype, w_dtype);
+  if (rc) return rc;
+  if (!w || !dw) return BLOTH_ERR_NULL;
+  if (M > 0 && (!dy || !z || !rstd || !dz)) return BLOTH_ERR_NULL;
+  const int64_t ld_g = dz_out ? lddz_out : N;
+  if ((rc = check_ld(M, N, {lddy, ld_g, ldz, lddz}))) return rc;
+  const bool vec = dz_out ? rows_vec_ok(dtype, N, {dy, dz_out, z, dz}, {lddy, lddz_out, ldz, lddz})
+                          : rows_vec_ok(dtype, N, {dy, z, dz}, {lddy, ldz, lddz});
+  if (!vec && N > kMaxScalarRow) return BLOTH_ERR_ALIGN;
+  RowArgs a = make_rows(M, N, 0.f, w, w_offset, w_dtype);
+  a.dy = dy;
+  a.lddy = lddy;
+  a.x = z;
+  a.ldx = ldz;
+  a.res = dz_out;
+  a.ldres = ld_g;
+  a.out = dz;
+  a.ldo = lddz;
+  a.rstd_in = rstd;
+  return dispatch_dtype(dtype, [&](auto t) {
+    return rows_bwd<decltype(t)>(a, kRowAdd, vec, workspace, workspace_bytes, dw,
+                                 as_stream(stream));
   });
 }
 

@@ -1,6 +1,7 @@
 // Row kernels: RMSNorm over rows of N, optionally followed by rotate-half
 // RoPE on the first 2*half columns with per-row cos/sin tables (the
-// reference's fused_norm_rope contract), forward and backward.
+// reference's fused_norm_rope contract) or preceded by a residual add
+// (z = x + r, stored, then normalised), forward and backward.
 //
 // Layout. A row group of TPR threads owns one row at a time; thread lt holds
 // vectors j = 0..VPT-1 at columns (j*TPR + lt)*VEC .. +VEC, so every
@@ -43,9 +44,21 @@ struct RowArgs {
   int cs_dt;
   int cs_vec;  // cos/sin rows aligned for VEC-wide loads
   int64_t half;
+  const void* res;   // kRowAdd: r (forward) or dz_out, z's gradient from the residual stream (backward; may be null)
+  int64_t ldres;
+  void* res_out;     // kRowAdd forward: z = x + r in x's type
+  int64_t ldres_out;
   int64_t M;
   int N;
   float eps;
+};
+
+// What a row kernel computes besides the RMSNorm.
+enum RowKind : int {
+  kRowNorm = 0,  // RMSNorm
+  kRowRope = 1,  // RMSNorm, then rotate-half RoPE with per-row cos/sin tables
+  kRowAdd = 2,   // z = x + r rounded to x's type and stored, then RMSNorm of z;
+                 // the backward adds dz_out to the RMSNorm gradient of z
 };
 
 // Weight of column c as the kernels apply it, w[c] + w_off, in fp32.
@@ -173,8 +186,10 @@ __device__ __forceinline__ void rope_rows_bwd(float (&d)[VEC], int c, const T* d
   }
 }
 
-template <typename T, int VEC, int TPR, int VPT, int RPC, bool ROPE>
+template <typename T, int VEC, int TPR, int VPT, int RPC, int KIND>
 __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_fwd_kernel(const RowArgs a) {
+  constexpr bool ROPE = KIND == kRowRope;
+  constexpr bool RES = KIND == kRowAdd;
   using RR = RowReduce<TPR, RPC>;
   __shared__ float red[RR::SMEM_FLOATS];
   const int grp = threadIdx.x / TPR;
@@ -195,6 +210,15 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_fwd_ke
       const int c = (j * TPR + lt) * VEC;
       if (valid && c < N) {
         xp[j] = ldg_pack<T, VEC>(xr + c);
+        if constexpr (RES) {  // z = x + r, rounded once to T, stored, normalised below
+          float f[VEC], g[VEC];
+          unpack(xp[j], f);
+          unpack(ldg_pack<T, VEC>(reinterpret_cast<const T*>(a.res) + row * a.ldres + c), g);
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) f[e] += g[e];
+          xp[j] = pack<T, VEC>(f);
+          stg_pack<T, VEC>(reinterpret_cast<T*>(a.res_out) + row * a.ldres_out + c, xp[j]);
+        }
       } else {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) xp[j].v[e] = from_f<T>(0.f);
@@ -234,8 +258,10 @@ __device__ __forceinline__ void acc_fma(double& acc, float a, float b) {
   acc = fma((double)a, (double)b, acc);
 }
 
-template <typename T, int VEC, int TPR, int VPT, int RPC, bool ROPE>
+template <typename T, int VEC, int TPR, int VPT, int RPC, int KIND>
 __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_kernel(const RowArgs a) {
+  constexpr bool ROPE = KIND == kRowRope;
+  constexpr bool RES = KIND == kRowAdd;
   using RR = RowReduce<TPR, RPC>;
   using AccT = typename AccOf<T>::type;
   __shared__ float red[RR::SMEM_FLOATS];
@@ -311,6 +337,14 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_ke
         ld_weight_vec<VEC>(a, c, wv, w);
 #pragma unroll
         for (int e = 0; e < VEC; ++e) o[e] = rstd * (dn[e] * w[e] - (xf[e] * rstd) * dot);
+        if constexpr (RES) {
+          if (a.res != nullptr) {
+            float g[VEC];
+            unpack(ldg_pack<T, VEC>(reinterpret_cast<const T*>(a.res) + row * a.ldres + c), g);
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) o[e] += g[e];
+          }
+        }
         stg_pack<T, VEC>(dxr + c, pack<T, VEC>(o));
       }
     }
@@ -395,9 +429,9 @@ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 // Number of CTAs (and partial rows) the backward uses for M rows of N:
 // one wave of resident CTAs, or fewer when there are fewer row blocks.
-template <typename T, int VEC, typename Cfg, bool ROPE>
+template <typename T, int VEC, typename Cfg, int KIND>
 int64_t row_bwd_grid(int64_t M) {
-  auto kern = row_bwd_kernel<T, VEC, Cfg::TPR, Cfg::VPT, Cfg::RPC, ROPE>;
+  auto kern = row_bwd_kernel<T, VEC, Cfg::TPR, Cfg::VPT, Cfg::RPC, KIND>;
   const int occ = occupancy((const void*)kern, Cfg::TPR * Cfg::RPC, row_bwd_smem<T, VEC, Cfg>());
   const int64_t wave = (int64_t)device_sm_count() * (occ > 0 ? occ : 1);
   const int64_t need = ceil_div(M, Cfg::RPC);
@@ -405,13 +439,14 @@ int64_t row_bwd_grid(int64_t M) {
 }
 
 // Host entry points (instantiated per element type in rows_<type>.cu).
+// kind: a RowKind; vec: every row pointer and stride allows 16-byte accesses.
 template <typename T>
-int rows_fwd(const RowArgs& a, bool rope, bool vec, cudaStream_t st);
+int rows_fwd(const RowArgs& a, int kind, bool vec, cudaStream_t st);
 template <typename T>
-int rows_bwd(const RowArgs& a, bool rope, bool vec, void* ws, size_t ws_bytes, void* dw,
+int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, void* dw,
              cudaStream_t st);
 template <typename T>
-size_t rows_bwd_workspace(int64_t M, int N, bool rope);
+size_t rows_bwd_workspace(int64_t M, int N, int kind);
 
 // Deterministic column sum of [P][N] accumulator partials into dw (w_dt).
 template <typename AccT>

@@ -7,10 +7,10 @@
 
 namespace bloth {
 
-template <typename T, int VEC, typename Cfg, bool ROPE>
+template <typename T, int VEC, typename Cfg, int KIND>
 int launch_row_fwd(const RowArgs& a, cudaStream_t st) {
   constexpr int BLOCK = Cfg::TPR * Cfg::RPC;
-  auto kern = row_fwd_kernel<T, VEC, Cfg::TPR, Cfg::VPT, Cfg::RPC, ROPE>;
+  auto kern = row_fwd_kernel<T, VEC, Cfg::TPR, Cfg::VPT, Cfg::RPC, KIND>;
   const int occ = occupancy((const void*)kern, BLOCK, 0);
   const int64_t wave = (int64_t)device_sm_count() * (occ > 0 ? occ : 1);
   const int64_t need = ceil_div(a.M, Cfg::RPC);
@@ -20,17 +20,17 @@ int launch_row_fwd(const RowArgs& a, cudaStream_t st) {
   return cuda_status(cudaGetLastError());
 }
 
-template <typename T, int VEC, typename Cfg, bool ROPE>
+template <typename T, int VEC, typename Cfg, int KIND>
 int launch_row_bwd(const RowArgs& a0, void* ws, size_t ws_bytes, void* dw, cudaStream_t st) {
   using AccT = typename AccOf<T>::type;
   constexpr int BLOCK = Cfg::TPR * Cfg::RPC;
-  const int64_t grid = row_bwd_grid<T, VEC, Cfg, ROPE>(a0.M);
+  const int64_t grid = row_bwd_grid<T, VEC, Cfg, KIND>(a0.M);
   if ((size_t)grid * a0.N * sizeof(AccT) > ws_bytes || (grid > 0 && ws == nullptr))
     return BLOTH_ERR_WORKSPACE;
   if (grid > 0) {
     RowArgs a = a0;
     a.partials = ws;
-    auto kern = row_bwd_kernel<T, VEC, Cfg::TPR, Cfg::VPT, Cfg::RPC, ROPE>;
+    auto kern = row_bwd_kernel<T, VEC, Cfg::TPR, Cfg::VPT, Cfg::RPC, KIND>;
     constexpr size_t smem = row_bwd_smem<T, VEC, Cfg>();
     kern<<<(unsigned)grid, BLOCK, smem, st>>>(a);
     const int rc = cuda_status(cudaGetLastError());
@@ -44,11 +44,11 @@ int launch_row_bwd(const RowArgs& a0, void* ws, size_t ws_bytes, void* dw, cudaS
 // within a per-CTA budget that leaves room for several CTAs per SM (72 KB for
 // 128-thread CTAs, 112 KB for 256, 200 KB for larger); nst == 0 when even
 // two slots do not fit (the register kernels then take the rows).
-template <typename T, typename PC, bool BWD>
-RowPipe pipe_plan(int N, bool contiguous) {
+template <typename T, typename PC>
+RowPipe pipe_plan(int N, int inputs, bool contiguous) {
   RowPipe pp;
   pp.row_bytes = N * (int)sizeof(T);
-  pp.slot_bytes = PC::RPC * pp.row_bytes * (BWD ? 2 : 1);
+  pp.slot_bytes = PC::RPC * pp.row_bytes * inputs;
   pp.contiguous = contiguous ? 1 : 0;
   pp.fault = fault_word();
   const size_t budget = PC::BLOCK <= 128 ? 72 * 1024 : (PC::BLOCK <= 256 ? 112 * 1024 : 200 * 1024);
@@ -65,9 +65,9 @@ inline size_t pipe_smem(const RowPipe& pp, int N) {
 
 // Grid of the pipelined kernel (one wave of resident CTAs or fewer), or -1 if
 // the kernel cannot be prepared on this device.
-template <typename T, int VEC, typename PC, bool ROPE, bool BWD>
+template <typename T, int VEC, typename PC, int KIND, bool BWD>
 int64_t row_pipe_grid(int64_t M, int N, const RowPipe& pp) {
-  auto kern = row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, ROPE, BWD>;
+  auto kern = row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, BWD>;
   const size_t smem = pipe_smem(pp, N);
   if (prepare_smem((const void*)kern, smem) != BLOTH_OK) return -1;
   const int occ = occupancy((const void*)kern, PC::BLOCK, smem);
@@ -76,28 +76,28 @@ int64_t row_pipe_grid(int64_t M, int N, const RowPipe& pp) {
   return need < wave ? (need > 0 ? need : 0) : wave;
 }
 
-template <typename T, int VEC, typename PC, bool ROPE>
+template <typename T, int VEC, typename PC, int KIND>
 int launch_row_pipe_fwd(const RowArgs& a, const RowPipe& pp, cudaStream_t st) {
-  const int64_t grid = row_pipe_grid<T, VEC, PC, ROPE, false>(a.M, a.N, pp);
+  const int64_t grid = row_pipe_grid<T, VEC, PC, KIND, false>(a.M, a.N, pp);
   if (grid < 0) return BLOTH_ERR_CUDA;
   if (grid == 0) return BLOTH_OK;
-  row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, ROPE, false>
+  row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, false>
       <<<(unsigned)grid, PC::BLOCK, pipe_smem(pp, a.N), st>>>(a, pp);
   return cuda_status(cudaGetLastError());
 }
 
-template <typename T, int VEC, typename PC, bool ROPE>
+template <typename T, int VEC, typename PC, int KIND>
 int launch_row_pipe_bwd(const RowArgs& a0, const RowPipe& pp, void* ws, size_t ws_bytes, void* dw,
                         cudaStream_t st) {
   using AccT = typename AccOf<T>::type;
-  const int64_t grid = row_pipe_grid<T, VEC, PC, ROPE, true>(a0.M, a0.N, pp);
+  const int64_t grid = row_pipe_grid<T, VEC, PC, KIND, true>(a0.M, a0.N, pp);
   if (grid < 0) return BLOTH_ERR_CUDA;
   if ((size_t)grid * a0.N * sizeof(AccT) > ws_bytes || (grid > 0 && ws == nullptr))
     return BLOTH_ERR_WORKSPACE;
   if (grid > 0) {
     RowArgs a = a0;
     a.partials = ws;
-    row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, ROPE, true>
+    row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, true>
         <<<(unsigned)grid, PC::BLOCK, pipe_smem(pp, a0.N), st>>>(a, pp);
     const int rc = cuda_status(cudaGetLastError());
     if (rc != BLOTH_OK) return rc;
@@ -106,87 +106,102 @@ int launch_row_pipe_bwd(const RowArgs& a0, const RowPipe& pp, void* ws, size_t w
                                 a0.w_dt, st);
 }
 
-template <typename T>
-int rows_fwd(const RowArgs& a, bool rope, bool vec, cudaStream_t st) {
-  constexpr int V = 16 / sizeof(T);
-  int rc = BLOTH_ERR_SHAPE;
-  auto go = [&](auto cfg, auto vecc) {
-    using C = decltype(cfg);
-    constexpr int VV = decltype(vecc)::value;
-    rc = rope ? launch_row_fwd<T, VV, C, true>(a, st) : launch_row_fwd<T, VV, C, false>(a, st);
-  };
-  if (vec) {
-    dispatch_row_cfg<V>(a.N, [&](auto cfg) {
-      using C = decltype(cfg);
-      using PC = PipeCfg<C::TPR, C::VPT>;
-      const RowPipe pp = pipe_plan<T, PC, false>(a.N, a.ldx == a.N);
-      if (pp.nst > 0)
-        rc = rope ? launch_row_pipe_fwd<T, V, PC, true>(a, pp, st)
-                  : launch_row_pipe_fwd<T, V, PC, false>(a, pp, st);
-      else
-        go(cfg, std::integral_constant<int, V>{});
-    });
-  } else {
-    dispatch_row_cfg<1>(a.N, [&](auto cfg) { go(cfg, std::integral_constant<int, 1>{}); });
+// Calls f(std::integral_constant<int, kind>{}) for a RowKind known at run time.
+template <typename F>
+int with_row_kind(int kind, F&& f) {
+  switch (kind) {
+    case kRowNorm: return f(std::integral_constant<int, kRowNorm>{});
+    case kRowRope: return f(std::integral_constant<int, kRowRope>{});
+    case kRowAdd: return f(std::integral_constant<int, kRowAdd>{});
+    default: return BLOTH_ERR_ARG;
   }
-  return rc;
+}
+
+// Every input row of the kind's tensors is adjacent to the next (ld == N), so
+// a block of rows moves as one bulk copy.
+inline bool rows_contiguous(const RowArgs& a, int kind, bool bwd) {
+  if (a.ldx != a.N) return false;
+  if (bwd && a.lddy != a.N) return false;
+  if (kind == kRowAdd && a.ldres != a.N) return false;
+  return true;
 }
 
 template <typename T>
-int rows_bwd(const RowArgs& a, bool rope, bool vec, void* ws, size_t ws_bytes, void* dw,
+int rows_fwd(const RowArgs& a, int kind, bool vec, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  return with_row_kind(kind, [&](auto kc) {
+    constexpr int K = decltype(kc)::value;
+    int rc = BLOTH_ERR_SHAPE;
+    if (vec) {
+      dispatch_row_cfg<V>(a.N, [&](auto cfg) {
+        using C = decltype(cfg);
+        using PC = PipeCfg<C::TPR, C::VPT>;
+        const RowPipe pp =
+            pipe_plan<T, PC>(a.N, row_pipe_inputs(K, false), rows_contiguous(a, K, false));
+        rc = pp.nst > 0 ? launch_row_pipe_fwd<T, V, PC, K>(a, pp, st)
+                        : launch_row_fwd<T, V, C, K>(a, st);
+      });
+    } else {
+      dispatch_row_cfg<1>(a.N, [&](auto cfg) { rc = launch_row_fwd<T, 1, decltype(cfg), K>(a, st); });
+    }
+    return rc;
+  });
+}
+
+template <typename T>
+int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, void* dw,
              cudaStream_t st) {
   constexpr int V = 16 / sizeof(T);
-  int rc = BLOTH_ERR_SHAPE;
-  auto go = [&](auto cfg, auto vecc) {
-    using C = decltype(cfg);
-    constexpr int VV = decltype(vecc)::value;
-    rc = rope ? launch_row_bwd<T, VV, C, true>(a, ws, ws_bytes, dw, st)
-              : launch_row_bwd<T, VV, C, false>(a, ws, ws_bytes, dw, st);
-  };
-  if (vec) {
-    dispatch_row_cfg<V>(a.N, [&](auto cfg) {
-      using C = decltype(cfg);
-      using PC = PipeCfg<C::TPR, C::VPT>;
-      const RowPipe pp = pipe_plan<T, PC, true>(a.N, a.ldx == a.N && a.lddy == a.N);
-      if (pp.nst > 0)
-        rc = rope ? launch_row_pipe_bwd<T, V, PC, true>(a, pp, ws, ws_bytes, dw, st)
-                  : launch_row_pipe_bwd<T, V, PC, false>(a, pp, ws, ws_bytes, dw, st);
-      else
-        go(cfg, std::integral_constant<int, V>{});
-    });
-  } else {
-    dispatch_row_cfg<1>(a.N, [&](auto cfg) { go(cfg, std::integral_constant<int, 1>{}); });
-  }
-  return rc;
+  // the residual add without a gradient from the residual stream is the plain backward
+  if (kind == kRowAdd && a.res == nullptr) kind = kRowNorm;
+  return with_row_kind(kind, [&](auto kc) {
+    constexpr int K = decltype(kc)::value;
+    int rc = BLOTH_ERR_SHAPE;
+    if (vec) {
+      dispatch_row_cfg<V>(a.N, [&](auto cfg) {
+        using C = decltype(cfg);
+        using PC = PipeCfg<C::TPR, C::VPT>;
+        const RowPipe pp =
+            pipe_plan<T, PC>(a.N, row_pipe_inputs(K, true), rows_contiguous(a, K, true));
+        rc = pp.nst > 0 ? launch_row_pipe_bwd<T, V, PC, K>(a, pp, ws, ws_bytes, dw, st)
+                        : launch_row_bwd<T, V, C, K>(a, ws, ws_bytes, dw, st);
+      });
+    } else {
+      dispatch_row_cfg<1>(a.N, [&](auto cfg) {
+        rc = launch_row_bwd<T, 1, decltype(cfg), K>(a, ws, ws_bytes, dw, st);
+      });
+    }
+    return rc;
+  });
 }
 
 // Workspace for the backward: the largest need of the pipelined, vector and
-// scalar paths, so the size does not depend on the pointers' alignment.
+// scalar paths of the kind (and of the plain kind the residual add falls back
+// to without dz_out), so the size depends on neither alignment nor dz_out.
 template <typename T>
-size_t rows_bwd_workspace(int64_t M, int N, bool rope) {
+size_t rows_bwd_workspace(int64_t M, int N, int kind) {
   using AccT = typename AccOf<T>::type;
   constexpr int V = 16 / sizeof(T);
   int64_t grid = 0;
-  auto take = [&](auto cfg, auto vecc) {
-    using C = decltype(cfg);
-    constexpr int VV = decltype(vecc)::value;
-    const int64_t g = rope ? row_bwd_grid<T, VV, C, true>(M) : row_bwd_grid<T, VV, C, false>(M);
+  auto take = [&](int64_t g) {
     if (g > grid) grid = g;
   };
-  dispatch_row_cfg<V>(N, [&](auto cfg) {
-    take(cfg, std::integral_constant<int, V>{});
-    using C = decltype(cfg);
-    using PC = PipeCfg<C::TPR, C::VPT>;
-    if (N % V == 0) {
-      const RowPipe pp = pipe_plan<T, PC, true>(N, true);
-      if (pp.nst > 0) {
-        const int64_t g = rope ? row_pipe_grid<T, V, PC, true, true>(M, N, pp)
-                               : row_pipe_grid<T, V, PC, false, true>(M, N, pp);
-        if (g > grid) grid = g;
+  auto one_kind = [&](auto kc) {
+    constexpr int K = decltype(kc)::value;
+    dispatch_row_cfg<V>(N, [&](auto cfg) {
+      using C = decltype(cfg);
+      using PC = PipeCfg<C::TPR, C::VPT>;
+      take(row_bwd_grid<T, V, C, K>(M));
+      if (N % V == 0) {
+        const RowPipe pp = pipe_plan<T, PC>(N, row_pipe_inputs(K, true), true);
+        if (pp.nst > 0) take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
       }
-    }
-  });
-  dispatch_row_cfg<1>(N, [&](auto cfg) { take(cfg, std::integral_constant<int, 1>{}); });
+    });
+    dispatch_row_cfg<1>(N, [&](auto cfg) { take(row_bwd_grid<T, 1, decltype(cfg), K>(M)); });
+    return 0;
+  };
+  with_row_kind(kind, one_kind);
+  if (kind == kRowAdd) with_row_kind(kRowNorm, one_kind);
   return (size_t)grid * (size_t)N * sizeof(AccT);
 }
 
@@ -194,8 +209,8 @@ size_t rows_bwd_workspace(int64_t M, int N, bool rope) {
 
 #define BLOTH_INSTANTIATE_ROWS(T)                                                   \
   namespace bloth {                                                                 \
-  template int rows_fwd<T>(const RowArgs&, bool, bool, cudaStream_t);               \
-  template int rows_bwd<T>(const RowArgs&, bool, bool, void*, size_t, void*,        \
+  template int rows_fwd<T>(const RowArgs&, int, bool, cudaStream_t);                \
+  template int rows_bwd<T>(const RowArgs&, int, bool, void*, size_t, void*,         \
                            cudaStream_t);                                           \
-  template size_t rows_bwd_workspace<T>(int64_t, int, bool);                        \
+  template size_t rows_bwd_workspace<T>(int64_t, int, int);                         \
   }

@@ -7,10 +7,11 @@
 // copy of block i + NST - 1 (one bulk copy of the whole block when the rows
 // are contiguous, else one per row from the lanes of warp 0) before the CTA
 // waits for block i, so NST - 1 blocks are in flight while one is computed.
-// A slot holds the block's x rows (forward) or dy rows then x rows
-// (backward); NST and the slot size are chosen on the host from N so that a
-// CTA uses at most ~200 KB of shared memory. The trailing __syncthreads of an
-// iteration releases its slot.
+// A slot holds the block's rows of each input tensor, one after another:
+// x (forward), dy then x (backward), and for the residual add x then r
+// (forward) or dy, z then dz_out (backward). NST and the slot size are chosen
+// on the host from N so that a CTA uses at most ~200 KB of shared memory. The
+// trailing __syncthreads of an iteration releases its slot.
 //
 // Math: as rows_impl.cuh (reference bloth/bloth/kernels/rms_norm.py:59-111,
 // fused_norm_qkv_rope.py:59-96); the RoPE partner half is read from the
@@ -25,7 +26,7 @@ namespace bloth {
 struct RowPipe {
   int nst;           // ring slots
   int row_bytes;     // N * sizeof(T), a multiple of 16
-  int slot_bytes;    // RPC * row_bytes * (1 forward, 2 backward)
+  int slot_bytes;    // RPC * row_bytes * (number of input tensors)
   int contiguous;    // rows of a block are adjacent in memory (ld == N) for every input
   unsigned int* fault;
 };
@@ -114,9 +115,17 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
   }
 }
 
-template <typename T, int VEC, int TPR, int VPT, int RPC, bool ROPE, bool BWD>
+// Input tensors a pipelined row kernel stages per row.
+constexpr int row_pipe_inputs(int kind, bool bwd) {
+  return (bwd ? 2 : 1) + (kind == kRowAdd ? 1 : 0);
+}
+
+template <typename T, int VEC, int TPR, int VPT, int RPC, int KIND, bool BWD>
 __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * RPC))
     row_pipe_kernel(const RowArgs a, const RowPipe pp) {
+  constexpr bool ROPE = KIND == kRowRope;
+  constexpr bool RES = KIND == kRowAdd;
+  constexpr int NTEN = row_pipe_inputs(KIND, BWD);
   using RR = RowReduce<TPR, RPC>;
   using AccT = typename AccOf<T>::type;
   __shared__ float red[RR::SMEM_FLOATS];
@@ -158,14 +167,15 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
     const int nrow = (int)min((int64_t)RPC, a.M - row0);
     unsigned char* dst = smem + (size_t)sl * pp.slot_bytes;
     uint64_t* bar = &bars[sl];
-    constexpr int NTEN = BWD ? 2 : 1;
     if (threadIdx.x == 0)
       mbar_arrive_expect_tx(bar, (uint32_t)(nrow * pp.row_bytes * NTEN));
     __syncwarp();
 #pragma unroll
     for (int q = 0; q < NTEN; ++q) {
-      const T* src = reinterpret_cast<const T*>(BWD && q == 0 ? a.dy : a.x);
-      const int64_t ld = BWD && q == 0 ? a.lddy : a.ldx;
+      // forward: x [, r]; backward: dy, x [, dz_out]
+      const int k = BWD ? q : q + 1;  // 0 dy, 1 x, 2 r / dz_out
+      const T* src = reinterpret_cast<const T*>(k == 0 ? a.dy : (k == 1 ? a.x : a.res));
+      const int64_t ld = k == 0 ? a.lddy : (k == 1 ? a.ldx : a.ldres);
       unsigned char* d = dst + (size_t)q * RPC * pp.row_bytes;
       if (pp.contiguous) {
         if (threadIdx.x == 0)
@@ -221,6 +231,20 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
         const int c = (j * TPR + lt) * VEC;
         if (valid && c < N) {
           xp[j] = lds_pack<T, VEC>(rowp + (int64_t)c * sizeof(T));
+          if constexpr (RES) {  // z = x + r, rounded once to T, stored, normalised below
+            float f[VEC], g[VEC];
+            unpack(xp[j], f);
+            unpack(lds_pack<T, VEC>(rowp + (size_t)RPC * pp.row_bytes + (int64_t)c * sizeof(T)),
+                   g);
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) {
+              const float2 z2 = f2_add(f2(f[e], f[e + 1]), f2(g[e], g[e + 1]));
+              f[e] = z2.x;
+              f[e + 1] = z2.y;
+            }
+            xp[j] = pack<T, VEC>(f);
+            stg_pack<T, VEC>(reinterpret_cast<T*>(a.res_out) + row * a.ldres_out + c, xp[j]);
+          }
         } else {
 #pragma unroll
           for (int e = 0; e < VEC; ++e) xp[j].v[e] = from_f<T>(0.f);
@@ -310,6 +334,17 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
                   f2_fma(x2, nd, f2_mul(f2(dn[e], dn[e + 1]), f2(wr[j][e], wr[j][e + 1]))), r2);
               o[e] = y.x;
               o[e + 1] = y.y;
+            }
+            if constexpr (RES) {  // dz = dz_out + the RMSNorm gradient of z
+              float g[VEC];
+              unpack(lds_pack<T, VEC>(xrp + (size_t)RPC * pp.row_bytes + (int64_t)c * sizeof(T)),
+                     g);
+#pragma unroll
+              for (int e = 0; e < VEC; e += 2) {
+                const float2 s2 = f2_add(f2(o[e], o[e + 1]), f2(g[e], g[e + 1]));
+                o[e] = s2.x;
+                o[e + 1] = s2.y;
+              }
             }
             stg_pack<T, VEC>(dxr + c, pack<T, VEC>(o));
           }

@@ -84,7 +84,7 @@ def _replace_norm_layers(model: nn.Module, verbose: bool = True) -> int:
 
 
 def patch_model(model: nn.Module, patch_norms: bool = True, patch_attention: bool = False,
-                verbose: bool = True) -> nn.Module:
+                verbose: bool = True, patch_residual: bool = False) -> nn.Module:
     """Applies the Bloth kernels to a HuggingFace model in place and returns it.
 
     patch_norms: replace RMSNorm layers (reference behaviour).
@@ -92,6 +92,8 @@ def patch_model(model: nn.Module, patch_norms: bool = True, patch_attention: boo
         supported attention modules through the fused kernels (Qwen3: one
         fused_qk_norm_rope launch; Llama / Mistral / Qwen2: one RoPE launch
         for q and k). The reference accepts this flag and does nothing.
+    patch_residual: fuse each decoder layer's attention residual add with its
+        post_attention_layernorm (fused_add_rms_norm). Not in the reference.
     """
     if verbose:
         print(f"\n[Bloth] Patching: {type(model).__name__}")
@@ -104,6 +106,9 @@ def patch_model(model: nn.Module, patch_norms: bool = True, patch_attention: boo
     if patch_attention:
         from .attention import patch_attention_layers
         total += patch_attention_layers(model, verbose)
+    if patch_residual:
+        from .attention import patch_decoder_layers
+        total += patch_decoder_layers(model, verbose)
     if total == 0 and verbose:
         warnings.warn("[Bloth] No layers patched. Architecture may not be recognised. "
                       "You can still use bloth_b200.kernels.* directly.")

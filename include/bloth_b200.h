@@ -117,6 +117,31 @@ int bloth_rmsnorm_bwd_noalloc(const void* dy, int64_t lddy, const void* x, int64
                               int64_t M, int64_t N, int dtype, int w_dtype, void* stream);
 
 /* ------------------------------------------------------------------------
+ * Residual add + RMSNorm over rows of N: z = x + r rounded to the type of x
+ * (stored: the decoder's residual stream), then y = z * rsqrt(mean(z^2) +
+ * eps) * (w + w_offset) in fp32, rounded once; rstd[M] fp32 saved. One pass
+ * over the rows instead of an add kernel and a norm kernel. z may be the same
+ * buffer as x or r (in place); other overlaps are undefined.
+ * No counterpart in the reference (which has no residual fusion): it fuses
+ * HF's `hidden_states = residual + hidden_states` with the
+ * post_attention_layernorm call that follows it in every Llama-family decoder
+ * layer (transformers models/llama/modeling_llama.py, LlamaDecoderLayer).
+ * ---------------------------------------------------------------------- */
+int bloth_add_rmsnorm_fwd(const void* x, int64_t ldx, const void* r, int64_t ldr, void* z,
+                          int64_t ldz, const void* w, float w_offset, void* y, int64_t ldy,
+                          float* rstd, int64_t M, int64_t N, float eps, int dtype, int w_dtype,
+                          void* stream);
+size_t bloth_add_rmsnorm_bwd_workspace_bytes(int64_t M, int64_t N, int dtype);
+/* Backward of bloth_add_rmsnorm_fwd: dz = dz_out + the RMSNorm gradient of z
+   for dy, which is the gradient of both x and r; dw as bloth_rmsnorm_bwd.
+   dz_out (the gradient reaching z from the rest of the residual stream) may
+   be NULL, meaning zero. dz may be the same buffer as dy or dz_out. */
+int bloth_add_rmsnorm_bwd(const void* dy, int64_t lddy, const void* dz_out, int64_t lddz_out,
+                          const void* z, int64_t ldz, const void* w, float w_offset,
+                          const float* rstd, void* dz, int64_t lddz, void* dw, int64_t M,
+                          int64_t N, int dtype, int w_dtype, void* workspace,
+                          size_t workspace_bytes, void* stream);
+/* ------------------------------------------------------------------------
  * Fused RMSNorm + rotate-half RoPE with per-row cos/sin tables, the
  * reference's fused_norm_rope(x, weight, cos, sin, eps) contract: each row of
  * N is RMS-normalised over all N columns; columns [0, 2*half) are rotated in

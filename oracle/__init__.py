@@ -14,6 +14,7 @@ from .reference_path import (  # noqa: F401
     rope_cos_sin,
     rms_norm,
     rms_norm_fwd_bwd,
+    add_rms_norm_fwd_bwd,
     norm_rope_table,
     norm_rope_table_fwd_bwd,
     norm_rope_table_reference_bwd,

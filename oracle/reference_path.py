@@ -109,6 +109,34 @@ def rms_norm_fwd_bwd(x, w, dy, eps: float = 1e-6, compute=F64, w_offset: float =
             xc.grad.to(x.dtype), wc.grad.to(w.dtype))
 
 
+# --------------------------------------------- residual add + RMSNorm
+def add_rms_norm_fwd_bwd(x, r, w, dy, dz_out=None, eps: float = 1e-6, compute=F64,
+                         w_offset: float = 0.0):
+    """Residual add then RMSNorm, as HF's decoder layer writes them
+    (transformers models/llama/modeling_llama.py, LlamaDecoderLayer.forward:
+    ``hidden_states = residual + hidden_states`` in the activations' dtype,
+    then ``post_attention_layernorm``), with the RMSNorm of :func:`rms_norm`;
+    forward and exact backward.
+
+    Returns y, z (x.dtype), rstd, dz (the gradient of both x and r; x.dtype)
+    and dw (w.dtype). dz_out is z's gradient from the residual stream (None:
+    zero).
+    """
+    xc = x.detach().to(compute).requires_grad_(True)
+    rc = r.detach().to(compute).requires_grad_(True)
+    wc = w.detach().to(compute).requires_grad_(True)
+    # torch adds 16-bit tensors in fp32 and rounds once to their dtype
+    z = (xc.float() + rc.float()).to(x.dtype).to(compute)
+    y, rstd = _rms_core(z, wc + w_offset, eps)
+    outs, grads = [y], [dy.to(compute)]
+    if dz_out is not None:
+        outs.append(z)
+        grads.append(dz_out.to(compute))
+    torch.autograd.backward(outs, grads)
+    return (y.detach().to(x.dtype), z.detach().to(x.dtype), rstd.detach().to(torch.float32),
+            xc.grad.to(x.dtype), wc.grad.to(w.dtype))
+
+
 # -------------------------------------------- fused norm + RoPE, row tables
 def norm_rope_table(x, w, cos, sin, eps: float = 1e-6, compute=F64):
     """Reference fused_norm_rope forward - fused_norm_qkv_rope.py:59-96.

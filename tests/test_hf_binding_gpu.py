@@ -212,3 +212,67 @@ def test_patched_model_generates_with_kv_cache(cuda):
     a = ref.generate(ids, max_new_tokens=8, do_sample=False)
     b = pat.generate(ids, max_new_tokens=8, do_sample=False)
     assert torch.equal(a, b)
+
+
+# ------------------------------------------------------ residual add + RMSNorm
+@pytest.mark.parametrize("dtype,M,N", [(torch.bfloat16, 333, 4096), (torch.float32, 300, 1024),
+                                       (torch.bfloat16, 97, 4100), (torch.bfloat16, 8, 65536),
+                                       (torch.float32, 8, 32768), (torch.float16, 64, 2048)])
+@pytest.mark.parametrize("with_dz", [True, False])
+def test_fused_add_rms_norm(cuda, dtype, M, N, with_dz):
+    x = seeded_normal((M, N), dtype, 40)
+    r = seeded_normal((M, N), dtype, 41)
+    w = seeded_weight(N, dtype, 42)
+    dy = seeded_normal((M, N), dtype, 43)
+    dz = seeded_normal((M, N), dtype, 44) if with_dz else None
+    ry, rz, _, rdx, rdw = oracle.add_rms_norm_fwd_bwd(x, r, w, dy, dz, 1e-6)
+    xg = x.to(cuda).requires_grad_(True)
+    rg = r.to(cuda).requires_grad_(True)
+    wg = w.to(cuda).requires_grad_(True)
+    y, z = bloth_b200.fused_add_rms_norm(xg, rg, wg, 1e-6)
+    outs, grads = [y], [dy.to(cuda)]
+    if with_dz:
+        outs.append(z)
+        grads.append(dz.to(cuda))
+    torch.autograd.backward(outs, grads)
+    assert torch.equal(z.cpu(), rz), "z = x + r must round exactly as the dtype's add"
+    assert_tol(y, ry, dtype, "y")
+    assert_tol(xg.grad, rdx, dtype, "dx")
+    assert_tol(rg.grad, rdx, dtype, "dr")
+    assert_tol(wg.grad, rdw, dtype, "dw", scale=True)
+
+
+def test_fused_add_rms_norm_in_place_through_the_abi(cuda):
+    from bloth_b200 import _lib
+    M, N = 500, 4096
+    x = seeded_normal((M, N), torch.bfloat16, 50)
+    r = seeded_normal((M, N), torch.bfloat16, 51)
+    w = seeded_weight(N, torch.bfloat16, 52)
+    ry, rz, rrs, _, _ = oracle.add_rms_norm_fwd_bwd(x, r, w, torch.zeros_like(x), None, 1e-5)
+    xd, rd, wd = x.to(cuda), r.to(cuda), w.to(cuda)
+    y = torch.empty_like(xd)
+    rstd = torch.empty(M, dtype=torch.float32, device=cuda)
+    lib = _lib.load()
+    rc = lib.bloth_add_rmsnorm_fwd(_lib.ptr(xd), N, _lib.ptr(rd), N, _lib.ptr(rd), N,
+                                   _lib.ptr(wd), 0.0, _lib.ptr(y), N, _lib.ptr(rstd), M, N, 1e-5,
+                                   _lib.BF16, _lib.BF16, _lib.stream_of(xd))
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert torch.equal(rd.cpu(), rz)  # the residual buffer now holds z
+    assert_tol(y, ry, torch.bfloat16, "y")
+    assert_tol(rstd, rrs, torch.float32, "rstd")
+
+
+@pytest.mark.parametrize("kind", ["qwen3", "llama"])
+def test_patched_residual_model_fp32_matches_hf(cuda, kind):
+    ref, pat = _tiny(kind, torch.float32, cuda)
+    bloth_b200.patch_model(pat, patch_attention=True, patch_residual=True, verbose=False)
+    ids = torch.randint(0, 128, (2, 48), device=cuda,
+                        generator=torch.Generator(device=cuda).manual_seed(4))
+    lr = ref(ids, labels=ids)
+    lp = pat(ids, labels=ids)
+    assert float((lr.logits - lp.logits).abs().max()) < 1e-4
+    lr.loss.backward()
+    lp.loss.backward()
+    for (n, a), (_, b) in zip(ref.named_parameters(), pat.named_parameters()):
+        assert float((a.grad - b.grad).abs().max()) < 1e-4, n

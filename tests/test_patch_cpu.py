@@ -133,3 +133,45 @@ def test_attention_binding_host_logic(monkeypatch, kind):
         ga = ref.generate(ids[:1], max_new_tokens=6, do_sample=False)
         gb = pat.generate(ids[:1], max_new_tokens=6, do_sample=False)
         assert torch.equal(ga, gb)
+
+
+@pytest.mark.parametrize("kind", ["qwen3", "llama"])
+def test_residual_binding_host_logic(monkeypatch, kind):
+    import oracle
+    from bloth_b200 import attention
+
+    def add_norm(x, r, w, eps=1e-6, weight_offset=0.0):
+        z = x + r
+        return oracle.rms_norm(z, w, eps, compute=torch.float32, w_offset=weight_offset)[0], z
+
+    monkeypatch.setattr(attention, "fused_add_rms_norm", add_norm)
+    _oracle_kernels(monkeypatch)
+    torch.manual_seed(0)
+    ref, pat = _tiny(kind), _tiny(kind)
+    pat.load_state_dict(ref.state_dict())
+    bloth_b200.patch_model(pat, patch_norms=False, patch_attention=True, patch_residual=True,
+                           verbose=False)
+    layers = [m for m in pat.modules() if type(m).__name__.endswith("DecoderLayer")]
+    assert len(layers) == 2 and all("forward" in m.__dict__ for m in layers)
+    ids = torch.randint(0, 64, (2, 20), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        a, b = ref(ids).logits, pat(ids).logits
+    assert float((a - b).abs().max()) < 1e-4
+    # a second call binds nothing more
+    assert attention.patch_decoder_layers(pat, verbose=False) == 0
+
+
+def test_add_rms_norm_oracle_gradients():
+    import oracle
+    g = torch.Generator().manual_seed(5)
+    x, r, dy, dz = (torch.randn(6, 32, generator=g, dtype=torch.float64) for _ in range(4))
+    w = torch.randn(32, generator=g, dtype=torch.float64)
+    y, z, _, dx, dw = oracle.add_rms_norm_fwd_bwd(x, r, w, dy, dz, 1e-6)
+    # against autograd of the unfused ops
+    xa, ra, wa = (t.clone().requires_grad_(True) for t in (x, r, w))
+    za = xa + ra
+    ya = za * torch.rsqrt((za * za).mean(-1, keepdim=True) + 1e-6) * wa
+    torch.autograd.backward([ya, za], [dy, dz])
+    assert torch.allclose(y, ya) and torch.allclose(z, za)
+    assert torch.allclose(dx, xa.grad) and torch.allclose(dx, ra.grad)
+    assert torch.allclose(dw, wa.grad)
