@@ -52,14 +52,20 @@ WORKLOADS = {
     "llama3-8b": (8, 4096, 4096, 32, 8, 128, 5e5, 1e-5, False),
     "llama3.2-1b": (4, 2048, 2048, 32, 8, 64, 5e5, 1e-5, False),
     "qwen3-8b-packed": (16, 8192, 0, 32, 8, 128, 1e6, 1e-6, True),
+    # as llama3-8b, with the hidden RMSNorm preceded by the residual add
+    # (fused_add_rms_norm: z = x + r, y = RMSNorm(z); z's gradient from the
+    # residual stream joins in the backward)
+    "llama3-8b-residual": (8, 4096, 4096, 32, 8, 128, 5e5, 1e-5, False),
 }
+RESIDUAL = {"llama3-8b-residual"}
 
 
 def describe(name: str) -> str:
     B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
     parts = []
     if Hd:
-        parts.append(f"hidden [{B},{S},{Hd}] RMSNorm")
+        parts.append(f"hidden [{B},{S},{Hd}] " +
+                     ("residual add + RMSNorm" if name in RESIDUAL else "RMSNorm"))
     parts.append(f"q [{B},{S},{Hq},{D}] + k [{B},{S},{Hk},{D}] norm+RoPE")
     extra = ", packed documents (lengths U[64,2048])" if packed else ""
     return f"{name}: " + " + ".join(parts) + f", bf16, theta {theta:g}, eps {eps:g}{extra}"
@@ -75,9 +81,15 @@ def step_bytes(tokens: int, name: str, elem: int = 2) -> dict:
     """
     _, _, Hd, Hq, Hk, D, _, _, _ = WORKLOADS[name]
     rows = Hq + Hk
+    if name in RESIDUAL:
+        # forward reads x, r and writes z, y; backward reads dy, z, dz_out and
+        # writes dz
+        hid = {"add_fwd": tokens * (4 * Hd * elem + 4), "add_bwd": tokens * (4 * Hd * elem + 4)}
+    else:
+        hid = {"rms_fwd": tokens * (2 * Hd * elem + 4) if Hd else 0,
+               "rms_bwd": tokens * (3 * Hd * elem + 4) if Hd else 0}
     out = {
-        "rms_fwd": tokens * (2 * Hd * elem + 4) if Hd else 0,
-        "rms_bwd": tokens * (3 * Hd * elem + 4) if Hd else 0,
+        **hid,
         "qk_fwd": tokens * (rows * (2 * D * elem + 4) + 8),
         "qk_bwd": tokens * (rows * (3 * D * elem + 4) + 8),
     }
@@ -126,6 +138,9 @@ def make_inputs(name: str, tokens_b: int, dev, seed: int, shard=(0, 1)):
         inp["x"] = randn(b, S, Hd)
         inp["w"] = weight(Hd)
         inp["gy"] = randn(b, S, Hd)
+        if name in RESIDUAL:
+            inp["r"] = randn(b, S, Hd)
+            inp["gz"] = randn(b, S, Hd)
     inp["q"] = randn(b, S, Hq, D)
     inp["k"] = randn(b, S, Hk, D)
     inp["wq"] = weight(D)
@@ -148,7 +163,15 @@ def run_step(inp, bloth):
     """One fwd+bwd pass through the public API; returns the gradients."""
     leaves = []
     outs, grads = [], []
-    if "x" in inp:
+    if "r" in inp:
+        x = inp["x"].requires_grad_(True)
+        r = inp["r"].requires_grad_(True)
+        w = inp["w"].requires_grad_(True)
+        y, z = bloth.fused_add_rms_norm(x, r, w, inp["eps"])
+        outs += [y, z]
+        grads += [inp["gy"], inp["gz"]]
+        leaves += [x, r, w]
+    elif "x" in inp:
         x = inp["x"].requires_grad_(True)
         w = inp["w"].requires_grad_(True)
         outs.append(bloth.rms_norm(x, w, inp["eps"]))
@@ -241,6 +264,9 @@ def cpu_port_step(name: str, tokens: int, seed: int = 0):
     x = torch.randn(t, Hd, generator=g).to(bf) if Hd else None
     w = (1 + 0.1 * torch.randn(Hd, generator=g)).to(bf) if Hd else None
     gy = torch.randn(t, Hd, generator=g).to(bf) if Hd else None
+    res = name in RESIDUAL
+    r = torch.randn(t, Hd, generator=g).to(bf) if res else None
+    gz = torch.randn(t, Hd, generator=g).to(bf) if res else None
     q = torch.randn(1, t, Hq, D, generator=g).to(bf)
     k = torch.randn(1, t, Hk, D, generator=g).to(bf)
     wq = (1 + 0.1 * torch.randn(D, generator=g)).to(bf)
@@ -252,7 +278,9 @@ def cpu_port_step(name: str, tokens: int, seed: int = 0):
     f32 = torch.float32
 
     def step():
-        if Hd:
+        if res:
+            oracle.add_rms_norm_fwd_bwd(x, r, w, gy, gz, eps, compute=f32)
+        elif Hd:
             oracle.rms_norm_fwd_bwd(x, w, gy, eps, compute=f32)
         oracle.qk_norm_rope_fwd_bwd(q, k, wq, wk, gq, gk, pos.view(1, t), inv, eps, compute=f32)
 
@@ -418,6 +446,7 @@ def main() -> None:
                    for k, v in per_kernel.items()) // unroll
     launches = per_step * steps
     kb = {"bloth_rmsnorm_fwd": "rms_fwd", "bloth_rmsnorm_bwd": "rms_bwd",
+          "bloth_add_rmsnorm_fwd": "add_fwd", "bloth_add_rmsnorm_bwd": "add_bwd",
           "bloth_qk_norm_rope_fwd": "qk_fwd", "bloth_qk_norm_rope_bwd": "qk_bwd"}
     top = max(per_kernel.items(), key=lambda kv: kv[1]["total_ms"])
     peaks = {}
@@ -486,7 +515,7 @@ def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
     are pipelined as a streaming user would: step i+1's inputs upload on a
     copy stream while step i computes, and step i's results download on a
     third stream (two device input buffers; events order every reuse)."""
-    keys_in = [k for k in ("x", "gy", "q", "k", "gq", "gk", "pos") if k in inp]
+    keys_in = [k for k in ("x", "r", "gy", "gz", "q", "k", "gq", "gk", "pos") if k in inp]
     host = {k: inp[k].detach().cpu().pin_memory() for k in keys_in}
     small = {k: v for k, v in inp.items() if k not in keys_in}
     h2d = sum(v.numel() * v.element_size() for v in host.values())

@@ -97,6 +97,24 @@ __device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint3
       : "memory");
 }
 
+// L2 policy that marks lines as first to evict: for inputs a kernel reads
+// exactly once, so that they do not displace lines still in use.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// bulk_load with an L2 cache policy (from evict_first_policy()).
+__device__ __forceinline__ void bulk_load_hint(void* dst_smem, const void* src, uint32_t bytes,
+                                               uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], "
+      "[%1], %2, [%3], %4;" ::"r"(smem_addr(dst_smem)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before
 // later async-proxy (bulk copy) accesses of the same memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -73,6 +73,19 @@ __device__ __forceinline__ void stg_pack(T* p, const Pack<T, VEC>& v) {
   *reinterpret_cast<Pack<T, VEC>*>(p) = v;
 }
 
+// Store with the streaming (evict-first) cache hint, for outputs this kernel
+// never reads back: their lines leave L2 for DRAM first, ahead of lines still
+// being filled. 16-byte packs only (p 16-byte aligned).
+template <typename T, int VEC>
+__device__ __forceinline__ void stg_pack_stream(T* p, const Pack<T, VEC>& v) {
+  static_assert(sizeof(Pack<T, VEC>) == 16, "streaming stores take 16-byte packs");
+  uint32_t w[4];
+  memcpy(w, &v, 16);
+  asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3])
+               : "memory");
+}
+
 template <typename T, int VEC>
 __device__ __forceinline__ void unpack(const Pack<T, VEC>& pk, float (&f)[VEC]) {
   if constexpr (std::is_same<T, __nv_bfloat16>::value && VEC % 2 == 0) {

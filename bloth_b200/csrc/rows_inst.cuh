@@ -40,21 +40,31 @@ int launch_row_bwd(const RowArgs& a0, void* ws, size_t ws_bytes, void* dw, cudaS
                                 a0.w_dt, st);
 }
 
-// Shared-memory plan of the pipelined row kernels for rows of N: ring slots
-// within a per-CTA budget that leaves room for several CTAs per SM (72 KB for
-// 128-thread CTAs, 112 KB for 256, 200 KB for larger); nst == 0 when even
-// two slots do not fit (the register kernels then take the rows).
+// Resident CTAs per SM of the pipelined row kernels (128-thread CTAs), by
+// what they compute. Measured on B200 at rows of 2048 and 4096 bf16 (same
+// optimum at both): fewer CTAs than the occupancy limit stream faster for the
+// kernels with two or three input tensors (e.g. the RMSNorm backward at 3 CTAs
+// per SM: 133.7 us at 32768 x 4096, against 154.8 us at 4 and 157.3 us at 2).
+constexpr int pipe_ctas_per_sm(int kind, bool bwd) {
+  return kind == kRowAdd ? (bwd ? 3 : 2) : (bwd ? 3 : 4);
+}
+
+// Shared-memory plan of the pipelined row kernels for rows of N: a
+// double-buffered ring (two slots: one block's copy in flight while the
+// previous block is computed), which measured 6-10% faster than three or four
+// slots at every row width tried; nst == 0 when two slots do not fit the
+// per-CTA budget (72 KB for 128-thread CTAs, 112 KB for 256, 200 KB for
+// larger), and the register kernels take the rows.
 template <typename T, typename PC>
-RowPipe pipe_plan(int N, int inputs, bool contiguous) {
+RowPipe pipe_plan(int N, int kind, bool bwd, bool contiguous) {
   RowPipe pp;
   pp.row_bytes = N * (int)sizeof(T);
-  pp.slot_bytes = PC::RPC * pp.row_bytes * inputs;
+  pp.slot_bytes = PC::RPC * pp.row_bytes * row_pipe_inputs(kind, bwd);
   pp.contiguous = contiguous ? 1 : 0;
   pp.fault = fault_word();
   const size_t budget = PC::BLOCK <= 128 ? 72 * 1024 : (PC::BLOCK <= 256 ? 112 * 1024 : 200 * 1024);
-  const size_t n = budget / ((size_t)pp.slot_bytes + 8);
-  pp.nst = n >= 4 ? 4 : (n >= 2 ? (int)n : 0);
-  (void)N;
+  pp.nst = 2 * ((size_t)pp.slot_bytes + 8) <= budget ? 2 : 0;
+  pp.ctas_per_sm = PC::BLOCK <= 128 ? pipe_ctas_per_sm(kind, bwd) : 0;
   return pp;
 }
 
@@ -70,8 +80,10 @@ int64_t row_pipe_grid(int64_t M, int N, const RowPipe& pp) {
   auto kern = row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, BWD>;
   const size_t smem = pipe_smem(pp, N);
   if (prepare_smem((const void*)kern, smem) != BLOTH_OK) return -1;
-  const int occ = occupancy((const void*)kern, PC::BLOCK, smem);
-  const int64_t wave = (int64_t)device_sm_count() * (occ > 0 ? occ : 1);
+  int occ = occupancy((const void*)kern, PC::BLOCK, smem);
+  if (occ < 1) occ = 1;
+  if (pp.ctas_per_sm > 0 && pp.ctas_per_sm < occ) occ = pp.ctas_per_sm;
+  const int64_t wave = (int64_t)device_sm_count() * occ;
   const int64_t need = ceil_div(M, PC::RPC);
   return need < wave ? (need > 0 ? need : 0) : wave;
 }
@@ -136,8 +148,7 @@ int rows_fwd(const RowArgs& a, int kind, bool vec, cudaStream_t st) {
       dispatch_row_cfg<V>(a.N, [&](auto cfg) {
         using C = decltype(cfg);
         using PC = PipeCfg<C::TPR, C::VPT>;
-        const RowPipe pp =
-            pipe_plan<T, PC>(a.N, row_pipe_inputs(K, false), rows_contiguous(a, K, false));
+        const RowPipe pp = pipe_plan<T, PC>(a.N, K, false, rows_contiguous(a, K, false));
         rc = pp.nst > 0 ? launch_row_pipe_fwd<T, V, PC, K>(a, pp, st)
                         : launch_row_fwd<T, V, C, K>(a, st);
       });
@@ -161,8 +172,7 @@ int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, vo
       dispatch_row_cfg<V>(a.N, [&](auto cfg) {
         using C = decltype(cfg);
         using PC = PipeCfg<C::TPR, C::VPT>;
-        const RowPipe pp =
-            pipe_plan<T, PC>(a.N, row_pipe_inputs(K, true), rows_contiguous(a, K, true));
+        const RowPipe pp = pipe_plan<T, PC>(a.N, K, true, rows_contiguous(a, K, true));
         rc = pp.nst > 0 ? launch_row_pipe_bwd<T, V, PC, K>(a, pp, ws, ws_bytes, dw, st)
                         : launch_row_bwd<T, V, C, K>(a, ws, ws_bytes, dw, st);
       });
@@ -193,7 +203,7 @@ size_t rows_bwd_workspace(int64_t M, int N, int kind) {
       using PC = PipeCfg<C::TPR, C::VPT>;
       take(row_bwd_grid<T, V, C, K>(M));
       if (N % V == 0) {
-        const RowPipe pp = pipe_plan<T, PC>(N, row_pipe_inputs(K, true), true);
+        const RowPipe pp = pipe_plan<T, PC>(N, K, true, true);
         if (pp.nst > 0) take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
       }
     });

@@ -28,8 +28,14 @@ struct RowPipe {
   int row_bytes;     // N * sizeof(T), a multiple of 16
   int slot_bytes;    // RPC * row_bytes * (number of input tensors)
   int contiguous;    // rows of a block are adjacent in memory (ld == N) for every input
+  int ctas_per_sm;   // resident CTAs per SM to launch (0: as many as fit)
   unsigned int* fault;
 };
+
+// Input tensors a pipelined row kernel stages per row.
+constexpr int row_pipe_inputs(int kind, bool bwd) {
+  return (bwd ? 2 : 1) + (kind == kRowAdd ? 1 : 0);
+}
 
 // CTA shape of the pipelined kernels: TPR threads per row and VPT vectors per
 // thread as the register kernels, but RPC = 128 / TPR rows per block (one
@@ -115,11 +121,6 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
   }
 }
 
-// Input tensors a pipelined row kernel stages per row.
-constexpr int row_pipe_inputs(int kind, bool bwd) {
-  return (bwd ? 2 : 1) + (kind == kRowAdd ? 1 : 0);
-}
-
 template <typename T, int VEC, int TPR, int VPT, int RPC, int KIND, bool BWD>
 __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * RPC))
     row_pipe_kernel(const RowArgs a, const RowPipe pp) {
@@ -159,6 +160,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
   const int64_t nblk = (a.M + RPC - 1) / RPC;
   const int64_t my_blk = blockIdx.x < nblk ? (nblk - 1 - blockIdx.x) / gridDim.x + 1 : 0;
 
+  const uint64_t pol = BWD ? 0ull : evict_first_policy();
   // Thread 0 (with the lanes of warp 0 for per-row copies) issues block i
   // into ring slot sl.
   auto issue = [&](int64_t i, int sl) {
@@ -177,12 +179,20 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
       const T* src = reinterpret_cast<const T*>(k == 0 ? a.dy : (k == 1 ? a.x : a.res));
       const int64_t ld = k == 0 ? a.lddy : (k == 1 ? a.ldx : a.ldres);
       unsigned char* d = dst + (size_t)q * RPC * pp.row_bytes;
+      // forward inputs are read once: evict-first in L2 (measured faster for
+      // the forward, slower for the backward, whose rows compete with dx)
       if (pp.contiguous) {
-        if (threadIdx.x == 0)
-          bulk_load(d, src + row0 * ld, (uint32_t)(nrow * pp.row_bytes), bar);
+        if (threadIdx.x == 0) {
+          if constexpr (BWD) bulk_load(d, src + row0 * ld, (uint32_t)(nrow * pp.row_bytes), bar);
+          else bulk_load_hint(d, src + row0 * ld, (uint32_t)(nrow * pp.row_bytes), bar, pol);
+        }
       } else if ((int)threadIdx.x < nrow) {
-        bulk_load(d + (size_t)threadIdx.x * pp.row_bytes, src + (row0 + threadIdx.x) * ld,
-                  (uint32_t)pp.row_bytes, bar);
+        if constexpr (BWD)
+          bulk_load(d + (size_t)threadIdx.x * pp.row_bytes, src + (row0 + threadIdx.x) * ld,
+                    (uint32_t)pp.row_bytes, bar);
+        else
+          bulk_load_hint(d + (size_t)threadIdx.x * pp.row_bytes, src + (row0 + threadIdx.x) * ld,
+                         (uint32_t)pp.row_bytes, bar, pol);
       }
     }
   };
