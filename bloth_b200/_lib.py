@@ -170,9 +170,10 @@ class LaunchTimer:
     created so that a CUDA-graph capture turns their records into event-record
     nodes, which re-record on every replay of the graph."""
 
-    def __init__(self, external: bool = False):
+    def __init__(self, external: bool = False, only=None):
         self.pairs: dict[str, list] = {}
         self.external = external
+        self.only = None if only is None else set(only)
 
     def _event(self):
         if self.external:
@@ -180,6 +181,8 @@ class LaunchTimer:
         return torch.cuda.Event(enable_timing=True)
 
     def wrap(self, name: str, t: torch.Tensor, fn):
+        if self.only is not None and name not in self.only:
+            return fn()
         s = torch.cuda.current_stream(t.device)
         a = self._event()
         b = self._event()
@@ -201,9 +204,11 @@ _timer: LaunchTimer | None = None
 
 
 @contextmanager
-def timing_launches(external: bool = False):
+def timing_launches(external: bool = False, only=None):
+    """Times every C-ABI launch made inside the block (or only those of the
+    entry points named in `only`)."""
     global _timer
-    prev, _timer = _timer, LaunchTimer(external)
+    prev, _timer = _timer, LaunchTimer(external, only)
     try:
         yield _timer
     finally:
