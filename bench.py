@@ -326,7 +326,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="llama3-8b", choices=sorted(WORKLOADS))
-    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-triton"])
     ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
@@ -357,6 +357,11 @@ def main() -> None:
                 "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
+        return
+
+    if args.impl == "reference-triton":
+        if rank == 0:
+            triton_reference(args, name)
         return
 
     import bloth_b200 as bloth
@@ -530,6 +535,85 @@ def main() -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def triton_reference(args, name: str) -> None:
+    """The reference's own GPU kernels (Triton) on the same workload, one GPU:
+    ``bloth.kernels.rms_norm`` on the hidden rows and
+    ``bloth.kernels.fused_norm_rope`` on the q and k head rows, forward and
+    backward, from the reference package installed under baseline/_ref. Its
+    fused contract takes one cos/sin row per normalised row, so the tables
+    are expanded across heads (bf16, as BlothRoPE caches them) before the
+    timed region: that work is not timed, in the reference's favour. Its
+    fused backward omits the transposed rotation, so this is a speed
+    reference only. Timed like the main arm: CUDA graphs of the step."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "bloth")):
+        print(json.dumps({"impl": "reference-triton",
+                          "unavailable": "reference not installed under baseline/_ref"}))
+        return
+    sys.path.insert(0, ref_dir)
+    import bloth as ref  # noqa: F401
+    from bloth.kernels import fused_norm_rope, rms_norm
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+    inp = make_inputs(name, B, dev, seed=1234)
+    ang = inp["pos"].to(torch.float32).unsqueeze(-1) * inp["inv_freq"]  # [B, S, D/2]
+    tabs = {}
+    for key, H in (("q", Hq), ("k", Hk)):
+        c = torch.cos(ang).to(torch.bfloat16).unsqueeze(2).expand(B, S, H, D // 2)
+        s_ = torch.sin(ang).to(torch.bfloat16).unsqueeze(2).expand(B, S, H, D // 2)
+        tabs[key] = (c.reshape(-1, D // 2).contiguous(), s_.reshape(-1, D // 2).contiguous())
+
+    def step():
+        outs, grads, leaves = [], [], []
+        if Hd:
+            x = inp["x"].requires_grad_(True)
+            w = inp["w"].requires_grad_(True)
+            outs.append(rms_norm(x, w, eps))
+            grads.append(inp["gy"])
+            leaves += [x, w]
+        for key, wkey, gkey in (("q", "wq", "gq"), ("k", "wk", "gk")):
+            t = inp[key].view(-1, D).requires_grad_(True)
+            w = inp[wkey].requires_grad_(True)
+            outs.append(fused_norm_rope(t, w, tabs[key][0], tabs[key][1], eps))
+            grads.append(inp[gkey].view(-1, D))
+            leaves += [t, w]
+        return torch.autograd.grad(outs, leaves, grads)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    unroll = next(u for u in (20, 10, 8, 5, 4, 2, 1) if args.steps % u == 0)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for _ in range(unroll):
+            step()
+    replays = max(1, args.steps // unroll)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(replays):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize(dev)
+    ms_step = start.elapsed_time(end) / (replays * unroll)
+    tokens = B * S
+    nbytes = step_bytes(tokens, name)["total"]
+    print(json.dumps({
+        "metric": METRIC, "impl": "reference-triton", "value": tokens / (ms_step / 1e3),
+        "unit": "tokens/s", "n_gpus": 1, "steps": replays * unroll, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": describe(name),
+                   "gbps": round(nbytes / (ms_step / 1e3) / 1e9, 1),
+                   "note": "reference Triton kernels (rms_norm, fused_norm_rope per row); "
+                           "cos/sin tables expanded per row before timing"}}), flush=True)
 
 
 def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
