@@ -331,6 +331,9 @@ def main() -> None:
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="bandwidth sweep over token counts (hidden 8192 and 32q/8k heads of "
+                         "128, bf16 and fp32); prints one JSON line, one GPU")
     ap.add_argument("--once", action="store_true",
                     help="run --warmup steps and one more fwd+bwd step, untimed, and exit "
                          "(a fixed launch sequence for profilers)")
@@ -357,6 +360,11 @@ def main() -> None:
                 "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line), flush=True)
+        return
+
+    if args.sweep:
+        if rank == 0:
+            sweep(args)
         return
 
     if args.impl == "reference-triton":
@@ -535,6 +543,89 @@ def main() -> None:
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def sweep(args) -> None:
+    """fwd+bwd GB/s of the hidden RMSNorm (rows of 8192) and of the q/k pair
+    (32 + 8 heads of 128, positions in-register) at token counts 2^14 .. 2^20
+    (bf16) and 2^14 .. 2^19 (fp32), each op alone in a CUDA graph of 10
+    steps. Sizes stop where the tensors of one op would approach 100 GB of
+    HBM; above a few times the L2 size the streaming rate is flat. Inputs
+    ~N(0, 1); rates do not depend on the values."""
+    import bloth_b200 as bloth
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = {}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            peaks = json.load(fh)
+    except OSError:
+        pass
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    Hd, Hq, Hk, D = 8192, 32, 8, 128
+    inv = (1.0 / (5e5 ** (torch.arange(0, D // 2, dtype=torch.float32) / (D // 2)))).to(dev)
+    points = []
+    for dt, top in ((torch.bfloat16, 20), (torch.float32, 19)):
+        s = torch.tensor([], dtype=dt).element_size()
+        for lg in range(14, top + 1, 2):
+            T = 1 << lg
+            g = torch.Generator(device=dev).manual_seed(lg)
+            for op in ("hidden", "qk"):
+                if op == "hidden":
+                    x = torch.randn(T, Hd, generator=g, device=dev, dtype=dt).requires_grad_(True)
+                    w = torch.ones(Hd, device=dev, dtype=dt).requires_grad_(True)
+                    gy = torch.randn(T, Hd, generator=g, device=dev, dtype=dt)
+                    nbytes = T * (5 * Hd * s + 8)
+
+                    def step():
+                        return torch.autograd.grad(bloth.rms_norm(x, w, 1e-6), (x, w), gy)
+                else:
+                    q = torch.randn(1, T, Hq, D, generator=g, device=dev,
+                                    dtype=dt).requires_grad_(True)
+                    k = torch.randn(1, T, Hk, D, generator=g, device=dev,
+                                    dtype=dt).requires_grad_(True)
+                    wq = torch.ones(D, device=dev, dtype=dt).requires_grad_(True)
+                    wk = torch.ones(D, device=dev, dtype=dt).requires_grad_(True)
+                    gq, gk = torch.randn_like(q), torch.randn_like(k)
+                    pos = (torch.arange(T, device=dev) % 8192).view(1, T)
+                    nbytes = T * ((Hq + Hk) * (5 * D * s + 8) + 16)
+
+                    def step():
+                        out = bloth.fused_qk_norm_rope(q, k, wq, wk, pos, inv, 1e-6)
+                        return torch.autograd.grad(out, (q, k, wq, wk), (gq, gk))
+                side = torch.cuda.Stream(dev)
+                side.wait_stream(torch.cuda.current_stream(dev))
+                with torch.cuda.stream(side):
+                    for _ in range(3):
+                        step()
+                torch.cuda.current_stream(dev).wait_stream(side)
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for _ in range(10):
+                        step()
+                graph.replay()
+                torch.cuda.synchronize(dev)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                reps = 3 if T >= (1 << 18) else 20
+                e0.record()
+                for _ in range(reps):
+                    graph.replay()
+                e1.record()
+                torch.cuda.synchronize(dev)
+                ms = e0.elapsed_time(e1) / (10 * reps)
+                gbps = nbytes / (ms / 1e3) / 1e9
+                points.append({"tokens": T, "dtype": str(dt).replace("torch.", ""), "op": op,
+                               "ms_fwd_bwd": round(ms, 4), "gbps": round(gbps, 1),
+                               "frac_of_measured": round(gbps / peak, 4),
+                               "tokens_per_s": round(T / (ms / 1e3))})
+                del graph
+                if op == "hidden":
+                    del x, w, gy
+                else:
+                    del q, k, wq, wk, gq, gk
+                torch.cuda.empty_cache()
+    print(json.dumps({"sweep": "fwd+bwd bandwidth vs size, one B200", "peak_gbs": peak,
+                      "points": points}), flush=True)
 
 
 def triton_reference(args, name: str) -> None:
