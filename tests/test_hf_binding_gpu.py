@@ -138,11 +138,11 @@ def test_apply_rotary_pos_emb_matches_hf(cuda, dtype):
 
 
 # ------------------------------------------------------------ whole models
-def _tiny(kind, dtype, dev, seed=0):
+def _tiny(kind, dtype, dev, seed=0, **extra):
     transformers = pytest.importorskip("transformers")
     torch.manual_seed(seed)
     common = dict(vocab_size=128, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
-                  num_attention_heads=4, num_key_value_heads=2)
+                  num_attention_heads=4, num_key_value_heads=2, **extra)
     if kind == "qwen3":
         cfg = transformers.Qwen3Config(head_dim=64, **common)
         cls = transformers.Qwen3ForCausalLM
@@ -198,9 +198,10 @@ def test_patched_model_bf16_no_worse_than_hf_bf16(cuda, kind):
     bloth_b200.patch_model(pat16, patch_attention=True, verbose=False)
     ids = torch.randint(0, 128, (2, 48), device=cuda,
                         generator=torch.Generator(device=cuda).manual_seed(2))
-    truth = ref32(ids).logits
-    err_hf = float((hf16(ids).logits.float() - truth).abs().max())
-    err_pat = float((pat16(ids).logits.float() - truth).abs().max())
+    with torch.no_grad():
+        truth = ref32(ids).logits
+        err_hf = float((hf16(ids).logits.float() - truth).abs().max())
+        err_pat = float((pat16(ids).logits.float() - truth).abs().max())
     assert err_pat <= 1.25 * err_hf + 1e-3, (err_pat, err_hf)
 
 
@@ -276,3 +277,87 @@ def test_patched_residual_model_fp32_matches_hf(cuda, kind):
     lp.loss.backward()
     for (n, a), (_, b) in zip(ref.named_parameters(), pat.named_parameters()):
         assert float((a.grad - b.grad).abs().max()) < 1e-4, n
+
+
+ROPE_PARAMS = {
+    "yarn": {"rope_type": "yarn", "factor": 4.0, "rope_theta": 1e4,
+             "original_max_position_embeddings": 32},
+    "llama3": {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+               "high_freq_factor": 4.0, "original_max_position_embeddings": 32,
+               "rope_theta": 5e5},
+    "linear": {"rope_type": "linear", "factor": 2.0, "rope_theta": 1e4},
+}
+
+
+def _compare(ref, pat, dev, seq=48, mask=None, grads=True, tol=1e-4):
+    ids = torch.randint(0, 128, (2, seq), device=dev,
+                        generator=torch.Generator(device=dev).manual_seed(7))
+    kw = {} if mask is None else {"attention_mask": mask}
+    lr = ref(ids, labels=ids, **kw)
+    lp = pat(ids, labels=ids, **kw)
+    keep = slice(None) if mask is None else mask.bool()
+    assert float((lr.logits[keep] - lp.logits[keep]).detach().abs().max()) < tol
+    if grads:
+        lr.loss.backward()
+        lp.loss.backward()
+        for (n, a), (_, b) in zip(ref.named_parameters(), pat.named_parameters()):
+            assert float((a.grad - b.grad).abs().max()) < tol, n
+
+
+@pytest.mark.parametrize("rope", sorted(ROPE_PARAMS))
+@pytest.mark.parametrize("kind", ["llama", "qwen3"])
+def test_patched_model_with_scaled_rope(cuda, kind, rope):
+    # HF's rotary embedding folds the rope type (and YaRN's attention_scaling
+    # != 1) into its cos/sin tables, which the binding reads as they are
+    ref, pat = _tiny(kind, torch.float32, cuda, rope_parameters=dict(ROPE_PARAMS[rope]))
+    bloth_b200.patch_model(pat, patch_attention=True, patch_residual=True, verbose=False)
+    _compare(ref, pat, cuda)
+
+
+def test_in_register_rope_scale_matches_hf_yarn_tables(cuda):
+    transformers = pytest.importorskip("transformers")
+    from transformers.models.llama import modeling_llama as ml
+    cfg = transformers.LlamaConfig(hidden_size=512, num_attention_heads=4, head_dim=128,
+                                   rope_parameters=dict(ROPE_PARAMS["yarn"]))
+    rot = ml.LlamaRotaryEmbedding(cfg).to(cuda)
+    assert abs(rot.attention_scaling - 1.0) > 0.1
+    B, S = 2, 200
+    pos = torch.arange(S, device=cuda).unsqueeze(0).expand(B, S)
+    cos, sin = rot(torch.zeros(1, device=cuda), pos)  # fp32 tables, scaling included
+    q = seeded_normal((B, S, 4, 128), torch.float32, 60).to(cuda)
+    k = seeded_normal((B, S, 2, 128), torch.float32, 61).to(cuda)
+    wq = seeded_weight(128, torch.float32, 62).to(cuda)
+    wk = seeded_weight(128, torch.float32, 63).to(cuda)
+    a = bloth_b200.fused_qk_norm_rope(q, k, wq, wk, pos, rot.inv_freq.float(), 1e-6,
+                                      rope_scale=rot.attention_scaling)
+    b = bloth_b200.fused_qk_norm_rope(q, k, wq, wk, None, None, 1e-6, cos=cos, sin=sin)
+    for x, y in zip(a, b):
+        assert float((x - y).abs().max()) < 1e-5
+
+
+def test_patched_mistral_sliding_window(cuda):
+    ref, pat = _tiny("mistral", torch.float32, cuda, sliding_window=16)
+    bloth_b200.patch_model(pat, patch_attention=True, patch_residual=True, verbose=False)
+    _compare(ref, pat, cuda, seq=48)
+
+
+def test_patched_model_left_padding(cuda):
+    ref, pat = _tiny("llama", torch.float32, cuda)
+    bloth_b200.patch_model(pat, patch_attention=True, patch_residual=True, verbose=False)
+    mask = torch.ones(2, 40, dtype=torch.long, device=cuda)
+    mask[0, :7] = 0  # left padding in the first sequence
+    with torch.no_grad():
+        _compare(ref, pat, cuda, seq=40, mask=mask, grads=False)
+
+
+def test_patched_model_fp16_no_worse_than_hf_fp16(cuda):
+    ref32, _ = _tiny("llama", torch.float32, cuda)
+    hf16, pat16 = _tiny("llama", torch.float16, cuda)
+    bloth_b200.patch_model(pat16, patch_attention=True, patch_residual=True, verbose=False)
+    ids = torch.randint(0, 128, (2, 48), device=cuda,
+                        generator=torch.Generator(device=cuda).manual_seed(8))
+    with torch.no_grad():
+        truth = ref32(ids).logits
+        err_hf = float((hf16(ids).logits.float() - truth).abs().max())
+        err_pat = float((pat16(ids).logits.float() - truth).abs().max())
+    assert err_pat <= 1.25 * err_hf + 1e-3, (err_pat, err_hf)

@@ -11,9 +11,9 @@ from bloth_b200.attention import _ATTENTION_CLASSES, _attention_forward
 transformers = pytest.importorskip("transformers")
 
 
-def _tiny(kind: str, head_dim: int = 64):
+def _tiny(kind: str, head_dim: int = 64, **extra):
     common = dict(vocab_size=64, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
-                  num_attention_heads=2, num_key_value_heads=1)
+                  num_attention_heads=2, num_key_value_heads=1, **extra)
     if kind == "qwen3":
         return transformers.Qwen3ForCausalLM(transformers.Qwen3Config(head_dim=head_dim, **common))
     if kind == "llama":
@@ -175,3 +175,22 @@ def test_add_rms_norm_oracle_gradients():
     assert torch.allclose(y, ya) and torch.allclose(z, za)
     assert torch.allclose(dx, xa.grad) and torch.allclose(dx, ra.grad)
     assert torch.allclose(dw, wa.grad)
+
+
+@pytest.mark.parametrize("kind,extra", [
+    ("llama", {"rope_parameters": {"rope_type": "yarn", "factor": 4.0, "rope_theta": 1e4,
+                                   "original_max_position_embeddings": 32}}),
+    ("qwen3", {"rope_parameters": {"rope_type": "linear", "factor": 2.0, "rope_theta": 1e4}}),
+    ("mistral", {"sliding_window": 8}),
+])
+def test_attention_binding_host_logic_variants(monkeypatch, kind, extra):
+    _oracle_kernels(monkeypatch)
+    torch.manual_seed(0)
+    ref, pat = _tiny(kind, **extra), _tiny(kind, **extra)
+    ref.config._attn_implementation = pat.config._attn_implementation = "eager"
+    pat.load_state_dict(ref.state_dict())
+    bloth_b200.patch_model(pat, patch_norms=False, patch_attention=True, verbose=False)
+    ids = torch.randint(0, 64, (2, 24), generator=torch.Generator().manual_seed(2))
+    with torch.no_grad():
+        a, b = ref(ids).logits, pat(ids).logits
+    assert float((a - b).abs().max()) < 1e-4
