@@ -769,9 +769,32 @@ def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
     barrier()
     ms = max_over_ranks(start.elapsed_time(end), dist, dev)
     d2h = sum(t.numel() * t.element_size() for t in outs_host)
+
+    # the same transfers alone (uploads on one stream, downloads of as many
+    # bytes on another, overlapped): the PCIe time the step cannot beat
+    dev_out = [torch.empty(h.shape, dtype=h.dtype, device=dev) for h in outs_host]
+    barrier()
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c0.record(s_main)
+    s_in.wait_stream(s_main)
+    s_out.wait_stream(s_main)
+    for i in range(steps):
+        with torch.cuda.stream(s_in):
+            for k in keys_in:
+                bufs[i % 2][k].copy_(host[k], non_blocking=True)
+        with torch.cuda.stream(s_out):
+            for h, t in zip(outs_host, dev_out):
+                h.copy_(t, non_blocking=True)
+    s_main.wait_stream(s_in)
+    s_main.wait_stream(s_out)
+    c1.record(s_main)
+    barrier()
+    copy_ms = max_over_ranks(c0.elapsed_time(c1), dist, dev)
     return {"value": tokens_total / (ms / steps / 1e3), "unit": "tokens/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": ms / steps}
+            "ms_per_step": ms / steps,
+            "transfers_only_ms_per_step": copy_ms / steps,
+            "h2d_plus_d2h_gbs": round((h2d + d2h) / (copy_ms / steps / 1e3) / 1e9, 1)}
 
 
 if __name__ == "__main__":
