@@ -11,6 +11,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
+from collections import OrderedDict
 from contextlib import contextmanager
 
 import torch
@@ -142,18 +143,28 @@ def stream_of(t: torch.Tensor) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
 
 
-_ws_cache: dict = {}
+_WS_CACHE_MAX = 4096
+_ws_cache: OrderedDict = OrderedDict()
+_ws_lock = threading.Lock()
 
 
 def workspace_bytes(entry: str, device: torch.device, *args) -> int:
     """Size reported by the C ABI's `entry` (a *_workspace_bytes function) on
-    `device`, cached: it depends only on the sizes and the device."""
+    `device`, cached (it depends only on the sizes and the device) in a
+    least-recently-used table of bounded size, so that shapes that vary from
+    step to step (packed batches) do not grow it without limit."""
     key = (entry, device.index, args)
-    v = _ws_cache.get(key)
-    if v is None:
-        with torch.cuda.device(device):
-            v = int(getattr(load(), entry)(*args))
+    with _ws_lock:
+        v = _ws_cache.get(key)
+        if v is not None:
+            _ws_cache.move_to_end(key)
+            return v
+    with torch.cuda.device(device):
+        v = int(getattr(load(), entry)(*args))
+    with _ws_lock:
         _ws_cache[key] = v
+        while len(_ws_cache) > _WS_CACHE_MAX:
+            _ws_cache.popitem(last=False)
     return v
 
 
@@ -200,6 +211,8 @@ class LaunchTimer:
         return out
 
 
+# Process-wide, not per thread: autograd runs backward on its own engine
+# thread, whose launches the timer must see too. One timing owner at a time.
 _timer: LaunchTimer | None = None
 
 

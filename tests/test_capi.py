@@ -180,3 +180,24 @@ def test_patch_model_swaps_norms_and_shares_weights():
     for n, m in after.items():
         assert m.weight is before[n]
     assert set(model.state_dict()) == keys
+
+
+def test_workspace_size_cache_is_bounded(monkeypatch):
+    calls = []
+
+    class FakeLib:
+        def fake_ws(self, *args):
+            calls.append(args)
+            return 64 * args[0]
+
+    monkeypatch.setattr(_lib, "load", lambda: FakeLib())
+    monkeypatch.setattr(_lib, "_WS_CACHE_MAX", 8)
+    monkeypatch.setattr(_lib, "_ws_cache", _lib.OrderedDict())
+    monkeypatch.setattr(torch.cuda, "device", lambda d: __import__("contextlib").nullcontext())
+    dev = torch.device("cpu")
+    for m in range(20):
+        assert _lib.workspace_bytes("fake_ws", dev, m, 4096, 1) == 64 * m
+    assert len(_lib._ws_cache) == 8
+    n = len(calls)
+    assert _lib.workspace_bytes("fake_ws", dev, 19, 4096, 1) == 64 * 19  # cached
+    assert len(calls) == n
