@@ -287,7 +287,10 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
               f[e + 1] = y.y;
             }
             if constexpr (ROPE) rope_pipe_fwd<T, VEC>(f, c, rowp, rstd, a, row);
-            stg_pack<T, VEC>(yr + c, pack<T, VEC>(f));
+            // streaming stores: 1.7% faster for the RMSNorm forward, none
+            // for the residual-add forward (measured on B200)
+            if constexpr (RES) stg_pack<T, VEC>(yr + c, pack<T, VEC>(f));
+            else stg_pack_stream<T, VEC>(yr + c, pack<T, VEC>(f));
           }
         }
       }
