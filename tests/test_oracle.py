@@ -1,6 +1,7 @@
 """Pins the CPU oracle against golden vectors produced by the reference's own
 Triton kernels (tests/golden/make_golden.py), and checks its internal
 consistency. CPU only."""
+import pytest
 import torch
 
 import oracle
@@ -142,3 +143,26 @@ def test_packed_position_ids_properties():
         assert all(64 <= n <= 2048 for n in lens)
         for a, n in zip(starts[:-1], lens):
             assert torch.equal(p[r, a:a + n], torch.arange(n))
+
+
+def test_gemma_norm_is_the_unit_offset_not_the_references_replacement():
+    # transformers' GemmaRMSNorm computes x_hat * (1 + w); the reference's
+    # patcher (bloth/bloth/patch.py:33-34 with :46-76) puts an x_hat * w norm
+    # in its place, which for Gemma's zero-initialised weights outputs zeros
+    transformers = pytest.importorskip("transformers")
+    from transformers.models.gemma.modeling_gemma import GemmaRMSNorm
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(16, 256, generator=g)
+    hf = GemmaRMSNorm(256, eps=1e-6)
+    with torch.no_grad():
+        hf.weight.normal_(0.0, 0.1, generator=g)
+        want = hf(x)
+    w = hf.weight.detach()
+    ours, _ = oracle.rms_norm(x, w, 1e-6, compute=torch.float32, w_offset=1.0)
+    assert torch.allclose(ours, want, atol=1e-6)
+    as_reference_patches_it, _ = oracle.rms_norm(x, w, 1e-6, compute=torch.float32)
+    assert float((as_reference_patches_it - want).abs().max()) > 0.5
+    fresh = GemmaRMSNorm(256, eps=1e-6)
+    with torch.no_grad():
+        assert float(oracle.rms_norm(x, fresh.weight, 1e-6)[0].abs().max()) == 0.0
+        assert float(fresh(x).abs().max()) > 1.0
