@@ -42,8 +42,8 @@ METRIC = "fused RMSNorm+RoPE fwd+bwd tokens/s and HBM GB/s (% of 8 TB/s) at 1/2/
 PROFILED_TRAFFIC = {
     ("llama3-8b", "bloth_qk_norm_rope_fwd"): 335_875_072 + 284_173_056,
     ("llama3-8b", "bloth_qk_norm_rope_bwd"): 677_358_336 + 301_042_176,
-    ("llama3-8b", "bloth_rmsnorm_fwd"): 268_479_744 + 211_189_504,
-    ("llama3-8b", "bloth_rmsnorm_bwd"): 537_066_496 + 239_095_040,
+    ("llama3-8b", "bloth_rmsnorm_fwd"): 268_540_416 + 214_617_600,
+    ("llama3-8b", "bloth_rmsnorm_bwd"): 537_134_848 + 238_408_704,
 }
 NOMINAL_HBM_GBS = 8000.0
 
