@@ -44,6 +44,7 @@ _SIGNATURES = {
     "bloth_strerror": (ctypes.c_char_p, [_int]),
     "bloth_last_cuda_error": (_int, []),
     "bloth_device_fault": (_int, [_int]),
+    "bloth_selftest_wait_expiry": (_int, [_int, _vp]),
     "bloth_rmsnorm_fwd": (_int, [_vp, _i64, _vp, _f32, _vp, _i64, _vp, _i64, _i64, _f32, _int,
                                  _int, _vp]),
     "bloth_rmsnorm_bwd_workspace_bytes": (_sz, [_i64, _i64, _int]),

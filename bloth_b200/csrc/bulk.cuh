@@ -73,12 +73,13 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // Waits for phase `parity` of `bar` to complete. Returns false (and records
 // kFaultCopyTimeout in *fault, the library's device fault word) if it has not
-// completed within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* fault) {
+// completed within limit_ns (kWaitLimitNs unless a caller asks for less).
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int* fault,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > limit_ns) {
       if (fault != nullptr) atomicOr(fault, kFaultCopyTimeout);
       return false;
     }

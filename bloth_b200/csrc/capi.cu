@@ -166,6 +166,10 @@ int bloth_last_cuda_error(void) { return bloth::last_cuda_error(); }
 
 int bloth_device_fault(int reset) { return bloth::device_fault(reset); }
 
+int bloth_selftest_wait_expiry(int limit_ms, void* stream) {
+  return bloth::selftest_wait_expiry(limit_ms, as_stream(stream));
+}
+
 // ---------------------------------------------------------------- RMSNorm
 int bloth_rmsnorm_fwd(const void* x, int64_t ldx, const void* w, float w_offset, void* y,
                       int64_t ldy,

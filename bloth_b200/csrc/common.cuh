@@ -245,5 +245,7 @@ int prepare_smem(const void* func, size_t smem);
 unsigned int* fault_word();
 // Records `err` as the calling thread's last CUDA error and maps it to a status.
 int cuda_status(cudaError_t err);
+// Launches the bounded-wait expiry check (bloth_selftest_wait_expiry).
+int selftest_wait_expiry(int limit_ms, cudaStream_t st);
 
 }  // namespace bloth

@@ -168,6 +168,26 @@ int launch_dw_reduce(const AccT* part, int64_t P, int N, void* dw0, int n0, void
 
 template int launch_dw_reduce<float>(const float*, int64_t, int, void*, int, void*, int,
                                      cudaStream_t);
+
+// One thread waits, with the pipelines' bounded wait, on a shared-memory
+// mbarrier that nothing will ever complete (no copy is issued, nothing
+// arrives), so the wait must give up after limit_ns and record
+// kFaultCopyTimeout. Exercises the timeout path on a real GPU without any
+// fault: nothing is in flight when the kernel returns.
+__global__ void wait_expiry_kernel(unsigned int* fault, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  mbar_init(&bar, 1);
+  mbar_init_fence();
+  (void)mbar_wait(&bar, 0, fault, limit_ns);
+}
+
+int selftest_wait_expiry(int limit_ms, cudaStream_t st) {
+  if (limit_ms < 1 || limit_ms > 2000) return BLOTH_ERR_ARG;
+  unsigned int* fault = fault_word();
+  if (fault == nullptr) return cuda_status(cudaErrorInvalidDevice);
+  wait_expiry_kernel<<<1, 1, 0, st>>>(fault, (unsigned long long)limit_ms * 1000000ull);
+  return cuda_status(cudaGetLastError());
+}
 template int launch_dw_reduce<double>(const double*, int64_t, int, void*, int, void*, int,
                                       cudaStream_t);
 

@@ -70,6 +70,13 @@ int bloth_last_cuda_error(void);
    kernel returned early; its outputs are invalid). Synchronises with the
    device; reset != 0 clears the bits. Negative on a CUDA error. */
 int bloth_device_fault(int reset);
+/* Diagnostic: launches one thread that waits, with the kernels' bounded
+   bulk-copy wait, on a barrier nothing completes, so the wait gives up after
+   limit_ms (1..2000) and sets fault bit 0 on the current device, as a real
+   expired copy would. Nothing is in flight when it returns, so the context
+   stays usable. Lets a deployment confirm that an expired wait ends the
+   kernel and reaches bloth_device_fault(). No counterpart in the reference. */
+int bloth_selftest_wait_expiry(int limit_ms, void* stream);
 
 /* ------------------------------------------------------------------------
  * RMSNorm over rows of N: y = x * rsqrt(mean(x^2) + eps) * w, computed in

@@ -201,3 +201,9 @@ def test_workspace_size_cache_is_bounded(monkeypatch):
     n = len(calls)
     assert _lib.workspace_bytes("fake_ws", dev, 19, 4096, 1) == 64 * 19  # cached
     assert len(calls) == n
+
+
+def test_wait_expiry_selftest_validates_its_limit_without_gpu():
+    lib = _lib.load()
+    assert lib.bloth_selftest_wait_expiry(0, None) == 7
+    assert lib.bloth_selftest_wait_expiry(5000, None) == 7
