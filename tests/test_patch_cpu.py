@@ -194,3 +194,22 @@ def test_attention_binding_host_logic_variants(monkeypatch, kind, extra):
     with torch.no_grad():
         a, b = ref(ids).logits, pat(ids).logits
     assert float((a - b).abs().max()) < 1e-4
+
+
+def test_fast_model_loads_a_local_checkpoint_and_patches_it(tmp_path):
+    # FastModel.from_pretrained (reference patch.py:133-200) against a model and
+    # tokenizer saved locally (no network); device_map=None keeps it on the CPU
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+    vocab = {"<unk>": 0, "<eos>": 1, **{f"w{i}": i + 2 for i in range(62)}}
+    tk = Tokenizer(models.WordLevel(vocab=vocab, unk_token="<unk>"))
+    tk.pre_tokenizer = pre_tokenizers.Whitespace()
+    PreTrainedTokenizerFast(tokenizer_object=tk, unk_token="<unk>",
+                            eos_token="<eos>").save_pretrained(tmp_path)
+    _tiny("qwen3").save_pretrained(tmp_path)
+    model, tok = bloth_b200.FastModel.from_pretrained(str(tmp_path), device_map=None,
+                                                      dtype=torch.float32)
+    assert tok.pad_token == tok.eos_token == "<eos>"
+    norms = [m for m in model.modules() if type(m).__name__ == "BlothRMSNorm"]
+    assert len(norms) == 9  # 2 layers x (input, post-attention, q_norm, k_norm) + final
+    assert next(model.parameters()).dtype == torch.float32
