@@ -657,54 +657,66 @@ def triton_reference(args, name: str) -> None:
         s_ = torch.sin(ang).to(torch.bfloat16).unsqueeze(2).expand(B, S, H, D // 2)
         tabs[key] = (c.reshape(-1, D // 2).contiguous(), s_.reshape(-1, D // 2).contiguous())
 
-    def step():
+    def step(norm, fused):
         outs, grads, leaves = [], [], []
         if Hd:
             x = inp["x"].requires_grad_(True)
             w = inp["w"].requires_grad_(True)
-            outs.append(rms_norm(x, w, eps))
+            outs.append(norm(x, w, eps))
             grads.append(inp["gy"])
             leaves += [x, w]
         for key, wkey, gkey in (("q", "wq", "gq"), ("k", "wk", "gk")):
             t = inp[key].view(-1, D).requires_grad_(True)
             w = inp[wkey].requires_grad_(True)
-            outs.append(fused_norm_rope(t, w, tabs[key][0], tabs[key][1], eps))
+            outs.append(fused(t, w, tabs[key][0], tabs[key][1], eps))
             grads.append(inp[gkey].view(-1, D))
             leaves += [t, w]
         return torch.autograd.grad(outs, leaves, grads)
 
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        for _ in range(max(args.warmup, 3)):
-            step()
-    torch.cuda.current_stream(dev).wait_stream(side)
-    torch.cuda.synchronize(dev)
-    unroll = next(u for u in (20, 10, 8, 5, 4, 2, 1) if args.steps % u == 0)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for _ in range(unroll):
-            step()
-    replays = max(1, args.steps // unroll)
-    graph.replay()
-    torch.cuda.synchronize(dev)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(replays):
+    def time_step(norm, fused):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(max(args.warmup, 3)):
+                step(norm, fused)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        unroll = next(u for u in (20, 10, 8, 5, 4, 2, 1) if args.steps % u == 0)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(unroll):
+                step(norm, fused)
+        replays = max(1, args.steps // unroll)
         graph.replay()
-    end.record()
-    torch.cuda.synchronize(dev)
-    ms_step = start.elapsed_time(end) / (replays * unroll)
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(replays):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize(dev)
+        return start.elapsed_time(end) / (replays * unroll), replays * unroll
+
+    ms_step, steps = time_step(rms_norm, fused_norm_rope)
+    # this build behind the same reference API, on the same inputs and tables
+    import bloth_b200
+    ms_b200, _ = time_step(bloth_b200.rms_norm, bloth_b200.kernels.fused_norm_rope)
     tokens = B * S
     nbytes = step_bytes(tokens, name)["total"]
     print(json.dumps({
         "metric": METRIC, "impl": "reference-triton", "value": tokens / (ms_step / 1e3),
-        "unit": "tokens/s", "n_gpus": 1, "steps": replays * unroll, "warmup": args.warmup,
+        "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": describe(name),
                    "gbps": round(nbytes / (ms_step / 1e3) / 1e9, 1),
                    "note": "reference Triton kernels (rms_norm, fused_norm_rope per row); "
-                           "cos/sin tables expanded per row before timing"}}), flush=True)
+                           "cos/sin tables expanded per row before timing",
+                   "same_api_b200": {"ms_per_step": ms_b200,
+                                     "tokens_per_s": tokens / (ms_b200 / 1e3),
+                                     "note": "bloth_b200.rms_norm and "
+                                             "bloth_b200.kernels.fused_norm_rope on the same "
+                                             "inputs and per-row tables (which it reads)"}}}),
+          flush=True)
 
 
 def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
