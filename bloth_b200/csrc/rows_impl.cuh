@@ -59,7 +59,14 @@ enum RowKind : int {
   kRowRope = 1,  // RMSNorm, then rotate-half RoPE with per-row cos/sin tables
   kRowAdd = 2,   // z = x + r rounded to x's type and stored, then RMSNorm of z;
                  // the backward adds dz_out to the RMSNorm gradient of z
+  kRowRopeVec = 3,  // kRowRope whose tables are staged in the ring and allow
+                    // vector access (pipelined kernels only: neither the global
+                    // table reads nor the per-element fallback are compiled)
 };
+
+constexpr bool row_rope(int kind) { return kind == kRowRope || kind == kRowRopeVec; }
+// The kind the register kernels run for `kind` (they have one table RoPE).
+constexpr int reg_kind(int kind) { return kind == kRowRopeVec ? kRowRope : kind; }
 
 // Weight of column c as the kernels apply it, w[c] + w_off, in fp32.
 __device__ __forceinline__ float ld_weight(const RowArgs& a, int64_t c) {
@@ -138,15 +145,15 @@ __device__ __forceinline__ void rope_rows_fwd(float (&o)[VEC], int c, const T* x
                                               const RowArgs& a, int64_t row) {
   const int64_t h = a.half;
   if (c >= 2 * h) return;
-  if (a.cs_vec && (h % VEC) == 0) {
+  if ((h % VEC) == 0) {
     const bool first = c < h;
     const int64_t pc = first ? c + h : c - h;
     const int64_t i = first ? c : c - h;
     float xp[VEC], wp[VEC], cs[VEC], sn[VEC];
     unpack(ldg_pack<T, VEC>(xr + pc), xp);
     ld_weight_vec<VEC>(a, pc, a.w_vec, wp);
-    ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, true, cs);
-    ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, true, sn);
+    ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, cs);
+    ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, sn);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
       const float np = xp[e] * rstd * wp[e];
@@ -168,14 +175,14 @@ __device__ __forceinline__ void rope_rows_bwd(float (&d)[VEC], int c, const T* d
                                               const RowArgs& a, int64_t row) {
   const int64_t h = a.half;
   if (c >= 2 * h) return;
-  if (a.cs_vec && (h % VEC) == 0) {
+  if ((h % VEC) == 0) {
     const bool first = c < h;
     const int64_t pc = first ? c + h : c - h;
     const int64_t i = first ? c : c - h;
     float dp[VEC], cs[VEC], sn[VEC];
     unpack(ldg_pack<T, VEC>(dyr + pc), dp);
-    ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, true, cs);
-    ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, true, sn);
+    ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, cs);
+    ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, sn);
 #pragma unroll
     for (int e = 0; e < VEC; ++e)
       d[e] = first ? (d[e] * cs[e] + dp[e] * sn[e]) : (d[e] * cs[e] - dp[e] * sn[e]);

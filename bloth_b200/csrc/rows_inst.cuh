@@ -57,19 +57,46 @@ constexpr int pipe_ctas_per_sm(int kind, bool bwd) {
 // 128-thread CTAs, 112 KB for 256, 200 KB for larger), and the register
 // kernels take the rows.
 template <typename T, typename PC>
-RowPipe pipe_plan(int N, int kind, bool bwd, bool contiguous) {
+RowPipe pipe_plan(int N, int kind, bool bwd, bool contiguous, const RowArgs* a = nullptr) {
   RowPipe pp;
   pp.row_bytes = N * (int)sizeof(T);
   pp.slot_bytes = PC::RPC * pp.row_bytes * row_pipe_inputs(kind, bwd);
   pp.contiguous = contiguous ? 1 : 0;
   pp.fault = fault_word();
+  pp.cs_row_bytes = 0;
+  pp.cs_ld_bytes = 0;
+  pp.cs_contiguous = 0;
   const size_t budget = PC::BLOCK <= 128 ? 72 * 1024 : (PC::BLOCK <= 256 ? 112 * 1024 : 200 * 1024);
   // narrow rows: three slots for the backward and for forward slots under
   // 8 KB, two otherwise (measured: rows of 512 bf16 forward, 87.2 vs 94.2 us)
-  const int want = PC::NARROW && (bwd || pp.slot_bytes < 8192) ? 3 : 2;
-  pp.nst = (size_t)want * ((size_t)pp.slot_bytes + 8) <= budget
-               ? want
-               : (2 * ((size_t)pp.slot_bytes + 8) <= budget ? 2 : 0);
+  auto slots = [&](size_t slot_bytes) {
+    const int want = PC::NARROW && (bwd || slot_bytes < 8192) ? 3 : 2;
+    if ((size_t)want * (slot_bytes + 8) <= budget) return want;
+    return 2 * (slot_bytes + 8) <= budget ? 2 : 0;
+  };
+  pp.nst = slots((size_t)pp.slot_bytes);
+  // Table RoPE: stage the block's cos and sin rows in the slot too (instead
+  // of a dependent global load per vector in the rotation) when they can be
+  // bulk-copied: 16-byte aligned rows whose length is a multiple of 16 bytes.
+  if (row_rope(kind) && a != nullptr && pp.nst > 0) {
+    const int es = a->cs_dt == BLOTH_F32 ? 4 : 2;
+    const int64_t row = a->half * es;
+    const int64_t ld = a->ldcs * es;
+    const bool aligned = reinterpret_cast<uintptr_t>(a->cos) % 16 == 0 &&
+                         reinterpret_cast<uintptr_t>(a->sin) % 16 == 0;
+    const size_t staged = (size_t)pp.slot_bytes + 2 * (size_t)PC::RPC * (size_t)row;
+    const int nst = slots(staged);
+    if (aligned && row % 16 == 0 && ld % 16 == 0 && row <= (1 << 20) && nst > 0) {
+      pp.cs_row_bytes = (int)row;
+      pp.cs_ld_bytes = ld;
+      pp.cs_contiguous = a->ldcs == a->half ? 1 : 0;
+      pp.slot_bytes = (int)staged;
+      pp.nst = nst;
+    }
+  }
+  // the staged-only kernel cannot run unstaged: leave those rows to the
+  // register kernels
+  if (kind == kRowRopeVec && pp.cs_row_bytes == 0) pp.nst = 0;
   pp.ctas_per_sm = PC::BLOCK <= 128 ? pipe_ctas_per_sm(kind, bwd) : 0;
   return pp;
 }
@@ -130,6 +157,7 @@ int with_row_kind(int kind, F&& f) {
   switch (kind) {
     case kRowNorm: return f(std::integral_constant<int, kRowNorm>{});
     case kRowRope: return f(std::integral_constant<int, kRowRope>{});
+    case kRowRopeVec: return f(std::integral_constant<int, kRowRopeVec>{});
     case kRowAdd: return f(std::integral_constant<int, kRowAdd>{});
     default: return BLOTH_ERR_ARG;
   }
@@ -144,9 +172,19 @@ inline bool rows_contiguous(const RowArgs& a, int kind, bool bwd) {
   return true;
 }
 
+// The pipelined kernels' table RoPE without the per-element fallback, when
+// the tables allow VEC-wide access everywhere.
+template <int V>
+int pipe_kind(const RowArgs& a, int kind, bool vec) {
+  if (kind != kRowRope || !vec || !a.cs_vec || a.half % V != 0) return kind;
+  const int es = a.cs_dt == BLOTH_F32 ? 4 : 2;  // staging needs 16-byte table rows
+  return (a.half * es) % 16 == 0 && (a.ldcs * es) % 16 == 0 ? kRowRopeVec : kind;
+}
+
 template <typename T>
 int rows_fwd(const RowArgs& a, int kind, bool vec, cudaStream_t st) {
   constexpr int V = 16 / sizeof(T);
+  kind = pipe_kind<V>(a, kind, vec);
   return with_row_kind(kind, [&](auto kc) {
     constexpr int K = decltype(kc)::value;
     int rc = BLOTH_ERR_SHAPE;
@@ -154,12 +192,14 @@ int rows_fwd(const RowArgs& a, int kind, bool vec, cudaStream_t st) {
       dispatch_row_cfg<V>(a.N, [&](auto cfg) {
         using C = decltype(cfg);
         using PC = PipeCfg<C::TPR, C::VPT>;
-        const RowPipe pp = pipe_plan<T, PC>(a.N, K, false, rows_contiguous(a, K, false));
+        const RowPipe pp = pipe_plan<T, PC>(a.N, K, false, rows_contiguous(a, K, false), &a);
         rc = pp.nst > 0 ? launch_row_pipe_fwd<T, V, PC, K>(a, pp, st)
-                        : launch_row_fwd<T, V, C, K>(a, st);
+                        : launch_row_fwd<T, V, C, reg_kind(K)>(a, st);
       });
     } else {
-      dispatch_row_cfg<1>(a.N, [&](auto cfg) { rc = launch_row_fwd<T, 1, decltype(cfg), K>(a, st); });
+      dispatch_row_cfg<1>(a.N, [&](auto cfg) {
+        rc = launch_row_fwd<T, 1, decltype(cfg), reg_kind(K)>(a, st);
+      });
     }
     return rc;
   });
@@ -171,6 +211,7 @@ int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, vo
   constexpr int V = 16 / sizeof(T);
   // the residual add without a gradient from the residual stream is the plain backward
   if (kind == kRowAdd && a.res == nullptr) kind = kRowNorm;
+  kind = pipe_kind<V>(a, kind, vec);
   return with_row_kind(kind, [&](auto kc) {
     constexpr int K = decltype(kc)::value;
     int rc = BLOTH_ERR_SHAPE;
@@ -178,13 +219,13 @@ int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, vo
       dispatch_row_cfg<V>(a.N, [&](auto cfg) {
         using C = decltype(cfg);
         using PC = PipeCfg<C::TPR, C::VPT>;
-        const RowPipe pp = pipe_plan<T, PC>(a.N, K, true, rows_contiguous(a, K, true));
+        const RowPipe pp = pipe_plan<T, PC>(a.N, K, true, rows_contiguous(a, K, true), &a);
         rc = pp.nst > 0 ? launch_row_pipe_bwd<T, V, PC, K>(a, pp, ws, ws_bytes, dw, st)
-                        : launch_row_bwd<T, V, C, K>(a, ws, ws_bytes, dw, st);
+                        : launch_row_bwd<T, V, C, reg_kind(K)>(a, ws, ws_bytes, dw, st);
       });
     } else {
       dispatch_row_cfg<1>(a.N, [&](auto cfg) {
-        rc = launch_row_bwd<T, 1, decltype(cfg), K>(a, ws, ws_bytes, dw, st);
+        rc = launch_row_bwd<T, 1, decltype(cfg), reg_kind(K)>(a, ws, ws_bytes, dw, st);
       });
     }
     return rc;
@@ -207,17 +248,24 @@ size_t rows_bwd_workspace(int64_t M, int N, int kind) {
     dispatch_row_cfg<V>(N, [&](auto cfg) {
       using C = decltype(cfg);
       using PC = PipeCfg<C::TPR, C::VPT>;
-      take(row_bwd_grid<T, V, C, K>(M));
+      take(row_bwd_grid<T, V, C, reg_kind(K)>(M));
       if (N % V == 0) {
-        const RowPipe pp = pipe_plan<T, PC>(N, K, true, true);
-        if (pp.nst > 0) take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
+        RowPipe pp = pipe_plan<T, PC>(N, K, true, true);
+        if (pp.nst > 0) {
+          take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
+          // two unstaged slots: the least shared memory any plan of this
+          // shape uses, so the most CTAs (staged tables may lower the count)
+          pp.nst = 2;
+          take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
+        }
       }
     });
-    dispatch_row_cfg<1>(N, [&](auto cfg) { take(row_bwd_grid<T, 1, decltype(cfg), K>(M)); });
+    dispatch_row_cfg<1>(N, [&](auto cfg) { take(row_bwd_grid<T, 1, decltype(cfg), reg_kind(K)>(M)); });
     return 0;
   };
   with_row_kind(kind, one_kind);
   if (kind == kRowAdd) with_row_kind(kRowNorm, one_kind);
+  if (kind == kRowRope) with_row_kind(kRowRopeVec, one_kind);
   return (size_t)grid * (size_t)N * sizeof(AccT);
 }
 

@@ -29,8 +29,47 @@ struct RowPipe {
   int slot_bytes;    // RPC * row_bytes * (number of input tensors)
   int contiguous;    // rows of a block are adjacent in memory (ld == N) for every input
   int ctas_per_sm;   // resident CTAs per SM to launch (0: as many as fit)
+  // Table RoPE: the block's cos and sin rows are staged in the slot after the
+  // input rows (cs_row_bytes = half * element size, 0: read from global).
+  int cs_row_bytes;
+  int64_t cs_ld_bytes;  // table row stride in bytes
+  int cs_contiguous;    // table rows adjacent (ld == half): one copy per block
   unsigned int* fault;
 };
+
+// Element i of a staged cos/sin row at p (element type dt).
+__device__ __forceinline__ float lds_any(const unsigned char* p, int64_t i, int dt) {
+  switch (dt) {
+    case BLOTH_BF16: return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+    case BLOTH_F16: return __half2float(reinterpret_cast<const __half*>(p)[i]);
+    default: return reinterpret_cast<const float*>(p)[i];
+  }
+}
+
+// Elements i .. i+VEC-1 of a staged cos/sin row (i a multiple of VEC, so the
+// access is aligned to VEC elements).
+template <int VEC>
+__device__ __forceinline__ void lds_any_vec(const unsigned char* p, int64_t i, int dt,
+                                            float (&out)[VEC]) {
+  if (dt == BLOTH_F32) {
+    static_assert(VEC % 4 == 0, "fp32 table reads take whole float4s");
+#pragma unroll
+    for (int q = 0; q < VEC / 4; ++q) {
+      const float4 v = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i)[q];
+      out[4 * q] = v.x;
+      out[4 * q + 1] = v.y;
+      out[4 * q + 2] = v.z;
+      out[4 * q + 3] = v.w;
+    }
+  } else if (dt == BLOTH_BF16) {
+    // copied by value into registers first: unpacking straight from the
+    // shared-memory reference read it byte by byte (16 loads per pack, each
+    // 2-way bank-conflicted across the warp's two rows; measured by ncu)
+    unpack(lds_pack<__nv_bfloat16, VEC>(p + i * 2), out);
+  } else {
+    unpack(lds_pack<__half, VEC>(p + i * 2), out);
+  }
+}
 
 // Input tensors a pipelined row kernel stages per row.
 constexpr int row_pipe_inputs(int kind, bool bwd) {
@@ -54,26 +93,41 @@ struct PipeCfg {
   static constexpr int MIN_BLOCKS = BLOCK >= 512 ? 1 : 512 / BLOCK;
 };
 
-template <typename T, int VEC>
+// csp / snp: this row's staged cos / sin (nullptr: read the tables in global
+// memory); wpv: the weights of the partner columns c +- half held in
+// registers by the caller (nullptr: load them).
+template <typename T, int VEC, bool CSV>
 __device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsigned char* rowp,
-                                              float rstd, const RowArgs& a, int64_t row) {
+                                              float rstd, const RowArgs& a, int64_t row,
+                                              const unsigned char* csp, const unsigned char* snp,
+                                              const float* wpv) {
   const int64_t h = a.half;
   if (c >= 2 * h) return;
-  if (a.cs_vec && (h % VEC) == 0) {
+  if (CSV || (h % VEC) == 0) {
     const bool first = c < h;
     const int64_t pc = first ? c + h : c - h;
     const int64_t i = first ? c : c - h;
     float xp[VEC], wp[VEC], cs[VEC], sn[VEC];
     unpack(lds_pack<T, VEC>(rowp + pc * (int64_t)sizeof(T)), xp);
-    ld_weight_vec<VEC>(a, pc, a.w_vec, wp);
-    ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, true, cs);
-    ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, true, sn);
+    if (wpv != nullptr) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) wp[e] = wpv[e];
+    } else {
+      ld_weight_vec<VEC>(a, pc, a.w_vec, wp);
+    }
+    if (CSV || csp != nullptr) {
+      lds_any_vec<VEC>(csp, i, a.cs_dt, cs);
+      lds_any_vec<VEC>(snp, i, a.cs_dt, sn);
+    } else if constexpr (!CSV) {
+      ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, cs);
+      ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, sn);
+    }
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
       const float np = xp[e] * rstd * wp[e];
       o[e] = first ? (o[e] * cs[e] - np * sn[e]) : (np * sn[e] + o[e] * cs[e]);
     }
-  } else {
+  } else if constexpr (!CSV) {
     const T* xr = reinterpret_cast<const T*>(rowp);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
@@ -83,31 +137,38 @@ __device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsi
         const int64_t pc = first ? cc + h : cc - h;
         const int64_t i = first ? cc : cc - h;
         const float np = to_f(xr[pc]) * rstd * ld_weight(a, pc);
-        const float cs = ld_any(a.cos, row * a.ldcs + i, a.cs_dt);
-        const float sn = ld_any(a.sin, row * a.ldcs + i, a.cs_dt);
+        const float cs = csp ? lds_any(csp, i, a.cs_dt) : ld_any(a.cos, row * a.ldcs + i, a.cs_dt);
+        const float sn = snp ? lds_any(snp, i, a.cs_dt) : ld_any(a.sin, row * a.ldcs + i, a.cs_dt);
         o[e] = first ? (o[e] * cs - np * sn) : (np * sn + o[e] * cs);
       }
     }
   }
 }
 
-template <typename T, int VEC>
+template <typename T, int VEC, bool CSV>
 __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsigned char* dyp,
-                                              const RowArgs& a, int64_t row) {
+                                              const RowArgs& a, int64_t row,
+                                              const unsigned char* csp,
+                                              const unsigned char* snp) {
   const int64_t h = a.half;
   if (c >= 2 * h) return;
-  if (a.cs_vec && (h % VEC) == 0) {
+  if (CSV || (h % VEC) == 0) {
     const bool first = c < h;
     const int64_t pc = first ? c + h : c - h;
     const int64_t i = first ? c : c - h;
     float dp[VEC], cs[VEC], sn[VEC];
     unpack(lds_pack<T, VEC>(dyp + pc * (int64_t)sizeof(T)), dp);
-    ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, true, cs);
-    ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, true, sn);
+    if (CSV || csp != nullptr) {
+      lds_any_vec<VEC>(csp, i, a.cs_dt, cs);
+      lds_any_vec<VEC>(snp, i, a.cs_dt, sn);
+    } else if constexpr (!CSV) {
+      ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, cs);
+      ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, sn);
+    }
 #pragma unroll
     for (int e = 0; e < VEC; ++e)
       d[e] = first ? (d[e] * cs[e] + dp[e] * sn[e]) : (d[e] * cs[e] - dp[e] * sn[e]);
-  } else {
+  } else if constexpr (!CSV) {
     const T* dr = reinterpret_cast<const T*>(dyp);
 #pragma unroll
     for (int e = 0; e < VEC; ++e) {
@@ -117,8 +178,8 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
         const int64_t pc = first ? cc + h : cc - h;
         const int64_t i = first ? cc : cc - h;
         const float dp = to_f(dr[pc]);
-        const float cs = ld_any(a.cos, row * a.ldcs + i, a.cs_dt);
-        const float sn = ld_any(a.sin, row * a.ldcs + i, a.cs_dt);
+        const float cs = csp ? lds_any(csp, i, a.cs_dt) : ld_any(a.cos, row * a.ldcs + i, a.cs_dt);
+        const float sn = snp ? lds_any(snp, i, a.cs_dt) : ld_any(a.sin, row * a.ldcs + i, a.cs_dt);
         d[e] = first ? (d[e] * cs + dp * sn) : (d[e] * cs - dp * sn);
       }
     }
@@ -128,7 +189,8 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
 template <typename T, int VEC, int TPR, int VPT, int RPC, int KIND, bool BWD>
 __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * RPC))
     row_pipe_kernel(const RowArgs a, const RowPipe pp) {
-  constexpr bool ROPE = KIND == kRowRope;
+  constexpr bool ROPE = row_rope(KIND);
+  constexpr bool CSV = KIND == kRowRopeVec;  // tables known to allow vector access
   constexpr bool RES = KIND == kRowAdd;
   constexpr int NTEN = row_pipe_inputs(KIND, BWD);
   using RR = RowReduce<TPR, RPC>;
@@ -147,8 +209,12 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
     mbar_init_fence();
   }
   // The thread's columns are the same for every row it processes: keep their
-  // weights in registers (VPT * VEC <= 32 for every pipelined shape).
+  // weights in registers (VPT * VEC <= 32 for every pipelined shape), and for
+  // the table RoPE on narrow rows those of their rotation partners (c +- half)
+  // too (wide rows load them per vector, as registers are short there).
+  constexpr bool WP_REG = ROPE && VPT * VEC <= 16;
   float wr[VPT][VEC];
+  float wpr[WP_REG ? VPT : 1][VEC];
 #pragma unroll
   for (int j = 0; j < VPT; ++j) {
     const int c = (j * TPR + lt) * VEC;
@@ -157,6 +223,15 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
     } else {
 #pragma unroll
       for (int e = 0; e < VEC; ++e) wr[j][e] = 0.f;
+    }
+    if constexpr (WP_REG) {
+      const int64_t h = a.half;
+      if (c < 2 * h && h % VEC == 0) {
+        ld_weight_vec<VEC>(a, c < h ? c + h : c - h, wv, wpr[j]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) wpr[j][e] = 0.f;
+      }
     }
   }
   __syncthreads();
@@ -173,9 +248,27 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
     const int nrow = (int)min((int64_t)RPC, a.M - row0);
     unsigned char* dst = smem + (size_t)sl * pp.slot_bytes;
     uint64_t* bar = &bars[sl];
+    const uint32_t cs_bytes = ROPE ? 2u * (uint32_t)nrow * (uint32_t)pp.cs_row_bytes : 0u;
     if (threadIdx.x == 0)
-      mbar_arrive_expect_tx(bar, (uint32_t)(nrow * pp.row_bytes * NTEN));
+      mbar_arrive_expect_tx(bar, (uint32_t)(nrow * pp.row_bytes * NTEN) + cs_bytes);
     __syncwarp();
+    if constexpr (ROPE) {  // the block's cos and sin rows, after the input rows
+      if (pp.cs_row_bytes > 0) {
+        unsigned char* cdst = dst + (size_t)RPC * pp.row_bytes * NTEN;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const unsigned char* src = reinterpret_cast<const unsigned char*>(q == 0 ? a.cos : a.sin);
+          unsigned char* d = cdst + (size_t)q * RPC * pp.cs_row_bytes;
+          if (pp.cs_contiguous) {
+            if (threadIdx.x == 0)
+              bulk_load(d, src + row0 * pp.cs_ld_bytes, (uint32_t)(nrow * pp.cs_row_bytes), bar);
+          } else if ((int)threadIdx.x < nrow) {
+            bulk_load(d + (size_t)threadIdx.x * pp.cs_row_bytes,
+                      src + (row0 + threadIdx.x) * pp.cs_ld_bytes, (uint32_t)pp.cs_row_bytes, bar);
+          }
+        }
+      }
+    }
 #pragma unroll
     for (int q = 0; q < NTEN; ++q) {
       // forward: x [, r]; backward: dy, x [, dz_out]
@@ -236,6 +329,14 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
       csl = 0;
       cph ^= 1u;
     }
+    const unsigned char* csp = nullptr;  // this row's staged cos and sin
+    const unsigned char* snp = nullptr;
+    if constexpr (ROPE) {
+      if (pp.cs_row_bytes > 0) {
+        csp = slot + (size_t)RPC * pp.row_bytes * NTEN + (size_t)grp * pp.cs_row_bytes;
+        snp = csp + (size_t)RPC * pp.cs_row_bytes;
+      }
+    }
     if constexpr (!BWD) {
       const unsigned char* rowp = slot + (size_t)grp * pp.row_bytes;
       Pack<T, VEC> xp[VPT];
@@ -290,7 +391,9 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
               f[e] = y.x;
               f[e + 1] = y.y;
             }
-            if constexpr (ROPE) rope_pipe_fwd<T, VEC>(f, c, rowp, rstd, a, row);
+            if constexpr (ROPE)
+              rope_pipe_fwd<T, VEC, CSV>(f, c, rowp, rstd, a, row, csp, snp,
+                                    WP_REG ? wpr[WP_REG ? j : 0] : nullptr);
             // streaming stores: 1.7% faster for the RMSNorm forward, none
             // for the residual-add forward (measured on B200)
             if constexpr (RES) stg_pack<T, VEC>(yr + c, pack<T, VEC>(f));
@@ -312,7 +415,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
           float xf[VEC], dn[VEC];
           unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
           unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
-          if constexpr (ROPE) rope_pipe_bwd<T, VEC>(dn, c, dyp, a, row);
+          if constexpr (ROPE) rope_pipe_bwd<T, VEC, CSV>(dn, c, dyp, a, row, csp, snp);
 #pragma unroll
           for (int e = 0; e < VEC; e += 2) {
             const float2 d2 = f2(dn[e], dn[e + 1]);
@@ -342,7 +445,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
             float xf[VEC], dn[VEC], o[VEC];
             unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
             unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
-            if constexpr (ROPE) rope_pipe_bwd<T, VEC>(dn, c, dyp, a, row);
+            if constexpr (ROPE) rope_pipe_bwd<T, VEC, CSV>(dn, c, dyp, a, row, csp, snp);
             const float2 nd = f2s(-dot);
 #pragma unroll
             for (int e = 0; e < VEC; e += 2) {
