@@ -251,8 +251,10 @@ size_t rows_bwd_workspace(int64_t M, int N, int kind) {
       take(row_bwd_grid<T, V, C, reg_kind(K)>(M));
       if (N % V == 0) {
         RowPipe pp = pipe_plan<T, PC>(N, K, true, true);
-        if (pp.nst > 0) {
-          take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
+        // the staged-table kernel's plan (nst 0 here, without tables) is made
+        // per call: count it too
+        if (pp.nst > 0 || K == kRowRopeVec) {
+          if (pp.nst > 0) take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
           // two unstaged slots: the least shared memory any plan of this
           // shape uses, so the most CTAs (staged tables may lower the count)
           pp.nst = 2;

@@ -94,8 +94,12 @@ struct PipeCfg {
 };
 
 // csp / snp: this row's staged cos / sin (nullptr: read the tables in global
-// memory); wpv: the weights of the partner columns c +- half held in
-// registers by the caller (nullptr: load them).
+// memory); wpv: the signed weights of the partner columns held in registers
+// by the caller (nullptr: load them).
+//
+// With the rotation's sign folded into the partner weight,
+//   y_c = n_c cos_i + x_p rstd w^s_p sin_i,  w^s_p = -w_{c+h} (c < h), w_{c-h} (c >= h),
+// which is two packed multiplies and one packed fma per element pair.
 template <typename T, int VEC, bool CSV>
 __device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsigned char* rowp,
                                               float rstd, const RowArgs& a, int64_t row,
@@ -114,6 +118,8 @@ __device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsi
       for (int e = 0; e < VEC; ++e) wp[e] = wpv[e];
     } else {
       ld_weight_vec<VEC>(a, pc, a.w_vec, wp);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) wp[e] = first ? -wp[e] : wp[e];
     }
     if (CSV || csp != nullptr) {
       lds_any_vec<VEC>(csp, i, a.cs_dt, cs);
@@ -122,10 +128,13 @@ __device__ __forceinline__ void rope_pipe_fwd(float (&o)[VEC], int c, const unsi
       ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, cs);
       ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, sn);
     }
+    const float2 r2 = f2s(rstd);
 #pragma unroll
-    for (int e = 0; e < VEC; ++e) {
-      const float np = xp[e] * rstd * wp[e];
-      o[e] = first ? (o[e] * cs[e] - np * sn[e]) : (np * sn[e] + o[e] * cs[e]);
+    for (int e = 0; e < VEC; e += 2) {
+      const float2 np = f2_mul(f2_mul(f2(xp[e], xp[e + 1]), r2), f2(wp[e], wp[e + 1]));
+      const float2 y = f2_fma(np, f2(sn[e], sn[e + 1]), f2_mul(f2(o[e], o[e + 1]), f2(cs[e], cs[e + 1])));
+      o[e] = y.x;
+      o[e + 1] = y.y;
     }
   } else if constexpr (!CSV) {
     const T* xr = reinterpret_cast<const T*>(rowp);
@@ -165,9 +174,15 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
       ld_any_vec<VEC>(a.cos, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, cs);
       ld_any_vec<VEC>(a.sin, row * a.ldcs + i, a.cs_dt, a.cs_vec != 0, sn);
     }
+    // dn_c = dy_c cos_i + s dy_p sin_i, s = +1 (c < h), -1 (c >= h)
+    const float2 sg = f2s(first ? 1.f : -1.f);
 #pragma unroll
-    for (int e = 0; e < VEC; ++e)
-      d[e] = first ? (d[e] * cs[e] + dp[e] * sn[e]) : (d[e] * cs[e] - dp[e] * sn[e]);
+    for (int e = 0; e < VEC; e += 2) {
+      const float2 y = f2_fma(f2_mul(f2(dp[e], dp[e + 1]), sg), f2(sn[e], sn[e + 1]),
+                              f2_mul(f2(d[e], d[e + 1]), f2(cs[e], cs[e + 1])));
+      d[e] = y.x;
+      d[e + 1] = y.y;
+    }
   } else if constexpr (!CSV) {
     const T* dr = reinterpret_cast<const T*>(dyp);
 #pragma unroll
@@ -186,8 +201,20 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
   }
 }
 
+// Minimum resident CTAs the register allocation must allow: three for the
+// staged-table RoPE backward of narrow rows with one vector per thread
+// (256-thread CTAs, at most 80 registers, no spills; measured 12% faster
+// than the 2 CTAs its 86-94 registers allowed; the other narrow backward
+// kinds fit in 80 registers anyway, and wider rows spill under that cap),
+// else enough for 384 threads.
+constexpr int row_pipe_min_ctas(int block, int vectors_per_thread, int kind, bool bwd) {
+  return bwd && kind == kRowRopeVec && block == 256 && vectors_per_thread == 1
+             ? 3
+             : (block >= 384 ? 1 : 384 / block);
+}
+
 template <typename T, int VEC, int TPR, int VPT, int RPC, int KIND, bool BWD>
-__global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * RPC))
+__global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KIND, BWD))
     row_pipe_kernel(const RowArgs a, const RowPipe pp) {
   constexpr bool ROPE = row_rope(KIND);
   constexpr bool CSV = KIND == kRowRopeVec;  // tables known to allow vector access
@@ -213,6 +240,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
   // the table RoPE on narrow rows those of their rotation partners (c +- half)
   // too (wide rows load them per vector, as registers are short there).
   constexpr bool WP_REG = ROPE && VPT * VEC <= 16;
+  constexpr bool KEEP = VPT * VEC <= 8;
   float wr[VPT][VEC];
   float wpr[WP_REG ? VPT : 1][VEC];
 #pragma unroll
@@ -224,10 +252,12 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
 #pragma unroll
       for (int e = 0; e < VEC; ++e) wr[j][e] = 0.f;
     }
-    if constexpr (WP_REG) {
+    if constexpr (WP_REG) {  // signed as rope_pipe_fwd expects
       const int64_t h = a.half;
       if (c < 2 * h && h % VEC == 0) {
         ld_weight_vec<VEC>(a, c < h ? c + h : c - h, wv, wpr[j]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) wpr[j][e] = c < h ? -wpr[j][e] : wpr[j][e];
       } else {
 #pragma unroll
         for (int e = 0; e < VEC; ++e) wpr[j][e] = 0.f;
@@ -408,6 +438,9 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
       // pass 1: dot = sum(dn*w*xhat), dweight terms dn*xhat
       float2 da = f2(0.f, 0.f), db = f2(0.f, 0.f);
       const float2 r2 = f2s(rstd);
+      // narrow rows keep dn and xhat in registers for pass 2 (instead of
+      // re-reading the slot and, for RoPE, rotating dy again)
+      float dnk[KEEP ? VPT : 1][VEC], xk[KEEP ? VPT : 1][VEC];
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int c = (j * TPR + lt) * VEC;
@@ -420,6 +453,12 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
           for (int e = 0; e < VEC; e += 2) {
             const float2 d2 = f2(dn[e], dn[e + 1]);
             const float2 x2 = f2_mul(f2(xf[e], xf[e + 1]), r2);
+            if constexpr (KEEP) {
+              dnk[KEEP ? j : 0][e] = d2.x;
+              dnk[KEEP ? j : 0][e + 1] = d2.y;
+              xk[KEEP ? j : 0][e] = x2.x;
+              xk[KEEP ? j : 0][e + 1] = x2.y;
+            }
             const float2 t = f2_mul(d2, f2(wr[j][e], wr[j][e + 1]));
             if ((e / 2) & 1) db = f2_fma(t, x2, db);
             else da = f2_fma(t, x2, da);
@@ -443,13 +482,22 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC >= 384 ? 1 : 384 / (TPR * 
           const int c = (j * TPR + lt) * VEC;
           if (c < N) {
             float xf[VEC], dn[VEC], o[VEC];
-            unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
-            unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
-            if constexpr (ROPE) rope_pipe_bwd<T, VEC, CSV>(dn, c, dyp, a, row, csp, snp);
+            if constexpr (KEEP) {
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) {
+                dn[e] = dnk[KEEP ? j : 0][e];
+                xf[e] = xk[KEEP ? j : 0][e];
+              }
+            } else {
+              unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
+              unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
+              if constexpr (ROPE) rope_pipe_bwd<T, VEC, CSV>(dn, c, dyp, a, row, csp, snp);
+            }
             const float2 nd = f2s(-dot);
 #pragma unroll
             for (int e = 0; e < VEC; e += 2) {
-              const float2 x2 = f2_mul(f2(xf[e], xf[e + 1]), r2);
+              // xf holds xhat already when kept
+              const float2 x2 = KEEP ? f2(xf[e], xf[e + 1]) : f2_mul(f2(xf[e], xf[e + 1]), r2);
               const float2 y = f2_mul(
                   f2_fma(x2, nd, f2_mul(f2(dn[e], dn[e + 1]), f2(wr[j][e], wr[j][e + 1]))), r2);
               o[e] = y.x;

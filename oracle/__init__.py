@@ -26,6 +26,7 @@ from .reference_path import (  # noqa: F401
     rms_norm_dw_scale,
     rms_norm_dx_scale,
     qk_dw_scale,
+    norm_rope_table_dw_scale,
     qk_dx_scale,
     tolerance_ok,
 )

@@ -326,6 +326,21 @@ def qk_dw_scale(x, dy, position_ids=None, inv_f=None, eps: float = 1e-6, cos=Non
     return torch.sqrt((t * t).reshape(-1, D).sum(0))
 
 
+def norm_rope_table_dw_scale(x, cos, sin, dy, eps: float = 1e-6, compute=F64):
+    """Per-column root-sum-square of the weight-gradient terms (R^T dy) * xhat
+    of :func:`norm_rope_table` (per-row tables; columns >= 2*half are not
+    rotated). See :func:`rms_norm_dw_scale`."""
+    h = cos.shape[-1]
+    g = dy.to(compute)
+    c, s = cos.to(compute), sin.to(compute)
+    g1, g2 = g[..., :h], g[..., h:2 * h]
+    dn = torch.cat([g1 * c + g2 * s, g2 * c - g1 * s, g[..., 2 * h:]], -1)
+    xc = x.to(compute)
+    rstd = 1.0 / torch.sqrt((xc * xc).mean(-1, keepdim=True) + eps)
+    t = dn * xc * rstd
+    return torch.sqrt((t * t).reshape(-1, x.shape[-1]).sum(0))
+
+
 def rms_norm_dx_scale(x, w, dy, eps: float = 1e-6, compute=F64, dy_mag=None):
     """Elementwise operand magnitude of dx = rstd * (dy*w - xhat*dot):
     rstd * (|dy|*|w| + |xhat*dot|). An fp32 evaluation of the difference
