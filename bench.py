@@ -35,15 +35,17 @@ if ROOT not in sys.path:
 
 METRIC = "fused RMSNorm+RoPE fwd+bwd tokens/s and HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
 
-# DRAM bytes (read + write) of one launch of each C-ABI call at the Llama-3-8B
-# shape, from the ncu captures summarised in profiles/ (cold L2, one launch of
-# the streaming kernel; a backward's dweight reduce launch moves under 1 MB and
-# is not included).
+# DRAM bytes (read + write) of one step's launches of each C-ABI call at the
+# Llama-3-8B shape, from the ncu captures summarised in profiles/ (cold L2; a
+# backward's dweight reduce launch moves under 1 MB and is not included).
 PROFILED_TRAFFIC = {
     ("llama3-8b", "bloth_qk_norm_rope_fwd"): 335_875_072 + 284_173_056,
     ("llama3-8b", "bloth_qk_norm_rope_bwd"): 677_358_336 + 301_042_176,
     ("llama3-8b", "bloth_rmsnorm_fwd"): 268_540_416 + 214_617_600,
     ("llama3-8b", "bloth_rmsnorm_bwd"): 537_134_848 + 238_408_704,
+    # reference-contract rows: the q and the k launch of the call together
+    ("llama3-8b-rows", "bloth_norm_rope_fwd"): 536_903_680 + 225_532_416 + 134_250_752 + 22_435_584,
+    ("llama3-8b-rows", "bloth_norm_rope_bwd"): 809_702_400 + 246_857_728 + 202_416_640 + 45_428_992,
 }
 NOMINAL_HBM_GBS = 8000.0
 
@@ -56,8 +58,14 @@ WORKLOADS = {
     # (fused_add_rms_norm: z = x + r, y = RMSNorm(z); z's gradient from the
     # residual stream joins in the backward)
     "llama3-8b-residual": (8, 4096, 4096, 32, 8, 128, 5e5, 1e-5, False),
+    # as llama3-8b, through the reference's own entry points: rms_norm, and
+    # fused_norm_rope on q and k as rows of head_dim with per-row cos/sin
+    # tables [rows, head_dim/2] (bf16, expanded across heads, as the
+    # reference's contract requires)
+    "llama3-8b-rows": (8, 4096, 4096, 32, 8, 128, 5e5, 1e-5, False),
 }
 RESIDUAL = {"llama3-8b-residual"}
+ROWS = {"llama3-8b-rows"}
 
 
 def describe(name: str) -> str:
@@ -66,7 +74,11 @@ def describe(name: str) -> str:
     if Hd:
         parts.append(f"hidden [{B},{S},{Hd}] " +
                      ("residual add + RMSNorm" if name in RESIDUAL else "RMSNorm"))
-    parts.append(f"q [{B},{S},{Hq},{D}] + k [{B},{S},{Hk},{D}] norm+RoPE")
+    if name in ROWS:
+        parts.append(f"q [{B},{S},{Hq},{D}] + k [{B},{S},{Hk},{D}] as rows of {D} through "
+                     f"fused_norm_rope with per-row bf16 cos/sin tables [rows, {D // 2}]")
+    else:
+        parts.append(f"q [{B},{S},{Hq},{D}] + k [{B},{S},{Hk},{D}] norm+RoPE")
     extra = ", packed documents (lengths U[64,2048])" if packed else ""
     return f"{name}: " + " + ".join(parts) + f", bf16, theta {theta:g}, eps {eps:g}{extra}"
 
@@ -77,7 +89,9 @@ def step_bytes(tokens: int, name: str, elem: int = 2) -> dict:
     Per normalised row of width W: forward reads x and writes y (2*W*s) and
     writes rstd (4 B); backward reads dy and x and writes dx (3*W*s) and reads
     rstd (4 B). Positions are int64: 8 B per token per pass. Weights and
-    dweight (a few KB) are not counted.
+    dweight (a few KB) are not counted. Through the per-row table contract
+    each head row also reads its cos and sin rows (2 * D/2 * s) in each pass,
+    and there are no positions.
     """
     _, _, Hd, Hq, Hk, D, _, _, _ = WORKLOADS[name]
     rows = Hq + Hk
@@ -88,11 +102,17 @@ def step_bytes(tokens: int, name: str, elem: int = 2) -> dict:
     else:
         hid = {"rms_fwd": tokens * (2 * Hd * elem + 4) if Hd else 0,
                "rms_bwd": tokens * (3 * Hd * elem + 4) if Hd else 0}
-    out = {
-        **hid,
-        "qk_fwd": tokens * (rows * (2 * D * elem + 4) + 8),
-        "qk_bwd": tokens * (rows * (3 * D * elem + 4) + 8),
-    }
+    if name in ROWS:
+        tab = 2 * (D // 2) * elem
+        out = {**hid,
+               "nr_fwd": tokens * rows * (2 * D * elem + 4 + tab),
+               "nr_bwd": tokens * rows * (3 * D * elem + 4 + tab)}
+    else:
+        out = {
+            **hid,
+            "qk_fwd": tokens * (rows * (2 * D * elem + 4) + 8),
+            "qk_bwd": tokens * (rows * (3 * D * elem + 4) + 8),
+        }
     out["total"] = sum(out.values())
     return out
 
@@ -156,6 +176,14 @@ def make_inputs(name: str, tokens_b: int, dev, seed: int, shard=(0, 1)):
     half = D // 2
     inp["inv_freq"] = (1.0 / (theta ** (torch.arange(0, half, dtype=torch.float32) / half))).to(dev)
     inp["eps"] = eps
+    if name in ROWS:
+        # per-row tables of the reference's contract: the angle of every
+        # (token, pair) evaluated in fp32, stored in bf16, expanded per head
+        ang = inp["pos"].to(torch.float32)[..., None] * inp["inv_freq"]
+        for key, H in (("q", Hq), ("k", Hk)):
+            for fn in ("cos", "sin"):
+                t = getattr(torch, fn)(ang).to(bf)[:, :, None, :].expand(b, S, H, half)
+                inp[f"{fn}_{key}"] = t.reshape(-1, half).contiguous()
     return inp
 
 
@@ -181,7 +209,11 @@ def run_step(inp, bloth):
     k = inp["k"].requires_grad_(True)
     wq = inp["wq"].requires_grad_(True)
     wk = inp["wk"].requires_grad_(True)
-    qo, ko = bloth.fused_qk_norm_rope(q, k, wq, wk, inp["pos"], inp["inv_freq"], inp["eps"])
+    if "cos_q" in inp:  # the reference's per-row table contract, one call per tensor
+        qo = bloth.kernels.fused_norm_rope(q, wq, inp["cos_q"], inp["sin_q"], inp["eps"])
+        ko = bloth.kernels.fused_norm_rope(k, wk, inp["cos_k"], inp["sin_k"], inp["eps"])
+    else:
+        qo, ko = bloth.fused_qk_norm_rope(q, k, wq, wk, inp["pos"], inp["inv_freq"], inp["eps"])
     outs += [qo, ko]
     grads += [inp["gq"], inp["gk"]]
     leaves += [q, k, wq, wk]
@@ -277,12 +309,26 @@ def cpu_port_step(name: str, tokens: int, seed: int = 0):
     inv = oracle.inv_freq(D, theta)
     f32 = torch.float32
 
+    tables = None
+    if name in ROWS:  # per-row bf16 tables, expanded across heads
+        ang = pos.to(f32)[:, None] * inv
+        tables = {key: [getattr(torch, fn)(ang).to(bf)[:, None, :].expand(t, H, D // 2)
+                        .reshape(-1, D // 2) for fn in ("cos", "sin")]
+                  for key, H in (("q", Hq), ("k", Hk))}
+
     def step():
         if res:
             oracle.add_rms_norm_fwd_bwd(x, r, w, gy, gz, eps, compute=f32)
         elif Hd:
             oracle.rms_norm_fwd_bwd(x, w, gy, eps, compute=f32)
-        oracle.qk_norm_rope_fwd_bwd(q, k, wq, wk, gq, gk, pos.view(1, t), inv, eps, compute=f32)
+        if tables is not None:
+            for rows, wt, gr, key in ((q, wq, gq, "q"), (k, wk, gk, "k")):
+                c, s_ = tables[key]
+                oracle.norm_rope_table_fwd_bwd(rows.reshape(-1, D), wt, c, s_,
+                                               gr.reshape(-1, D), eps, compute=f32)
+        else:
+            oracle.qk_norm_rope_fwd_bwd(q, k, wq, wk, gq, gk, pos.view(1, t), inv, eps,
+                                        compute=f32)
 
     return step
 
@@ -332,8 +378,9 @@ def main() -> None:
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--sweep", action="store_true",
-                    help="bandwidth sweep over token counts (hidden 8192 and 32q/8k heads of "
-                         "128, bf16 and fp32); prints one JSON line, one GPU")
+                    help="bandwidth sweep over token counts 2^14..2^24 (hidden 8192 and "
+                         "32q/8k heads of 128, bf16 and fp32; chunked above the resident "
+                         "sizes); prints one JSON line, one GPU")
     ap.add_argument("--once", action="store_true",
                     help="run --warmup steps and one more fwd+bwd step, untimed, and exit "
                          "(a fixed launch sequence for profilers)")
@@ -457,8 +504,11 @@ def main() -> None:
         end.record()
         barrier()
     ms = max_over_ranks(start.elapsed_time(end), dist, dev)
-    dom_ms = [a.elapsed_time(b) for tm in timers for a, b in tm.pairs[dominant]]
-    dom_ms = sorted(dom_ms)[len(dom_ms) // 2]  # median over the last replay's samples
+    # the dominant call's time per step (summed over its launches in the step:
+    # the table contract calls it once for q and once for k), median over the
+    # last replay's instrumented steps
+    dom_ms = sorted(sum(a.elapsed_time(b) for a, b in tm.pairs[dominant]) for tm in timers)
+    dom_ms = dom_ms[len(dom_ms) // 2]
     ms_step = ms / steps
     tokens_total = tokens_local * world
     value = tokens_total / (ms_step / 1e3)
@@ -482,7 +532,8 @@ def main() -> None:
     launches = per_step * steps
     kb = {"bloth_rmsnorm_fwd": "rms_fwd", "bloth_rmsnorm_bwd": "rms_bwd",
           "bloth_add_rmsnorm_fwd": "add_fwd", "bloth_add_rmsnorm_bwd": "add_bwd",
-          "bloth_qk_norm_rope_fwd": "qk_fwd", "bloth_qk_norm_rope_bwd": "qk_bwd"}
+          "bloth_qk_norm_rope_fwd": "qk_fwd", "bloth_qk_norm_rope_bwd": "qk_bwd",
+          "bloth_norm_rope_fwd": "nr_fwd", "bloth_norm_rope_bwd": "nr_bwd"}
     top = (dominant, {"mean_ms": dom_ms})
     peaks = {}
     try:
@@ -494,7 +545,7 @@ def main() -> None:
     top_bytes = nbytes[kb[top[0]]]
     achieved = top_bytes / (top[1]["mean_ms"] / 1e3) / 1e9
     kernels = {k: {"launches": v["launches"], "mean_us": round(v["mean_ms"] * 1e3, 2),
-                   "gbps": round(nbytes[kb[k]] / (v["mean_ms"] / 1e3) / 1e9, 1)}
+                   "gbps": round(nbytes[kb[k]] / (v["total_ms"] / 1e3) / 1e9, 1)}
                for k, v in per_kernel.items()}
 
     # ---- end to end through the public API with host buffers
@@ -547,11 +598,15 @@ def main() -> None:
 
 def sweep(args) -> None:
     """fwd+bwd GB/s of the hidden RMSNorm (rows of 8192) and of the q/k pair
-    (32 + 8 heads of 128, positions in-register) at token counts 2^14 .. 2^20
-    (bf16) and 2^14 .. 2^19 (fp32), each op alone in a CUDA graph of 10
-    steps. Sizes stop where the tensors of one op would approach 100 GB of
-    HBM; above a few times the L2 size the streaming rate is flat. Inputs
-    ~N(0, 1); rates do not depend on the values."""
+    (32 + 8 heads of 128, positions in-register) at token counts 2^14 .. 2^24,
+    bf16 and fp32, each op alone in a CUDA graph of 10 steps. Tensors stay
+    resident up to 2^20 tokens (bf16) / 2^18 (fp32), where one op holds
+    ~40-70 GB of HBM. Larger counts (a hidden fp32 tensor at 2^24 tokens is
+    550 GB) run chunked, as rows are independent: 2^(lg - top) chunks of the
+    largest resident size through the same device buffers, in a graph of one
+    such step. Every chunk's tensors are many times the L2 size, so reusing
+    the buffers saves no traffic. Inputs ~N(0, 1); rates do not depend on
+    the values."""
     import bloth_b200 as bloth
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -565,11 +620,12 @@ def sweep(args) -> None:
     Hd, Hq, Hk, D = 8192, 32, 8, 128
     inv = (1.0 / (5e5 ** (torch.arange(0, D // 2, dtype=torch.float32) / (D // 2)))).to(dev)
     points = []
-    for dt, top in ((torch.bfloat16, 20), (torch.float32, 19)):
+    for dt, top in ((torch.bfloat16, 20), (torch.float32, 18)):
         s = torch.tensor([], dtype=dt).element_size()
-        for lg in range(14, top + 1, 2):
-            T = 1 << lg
-            g = torch.Generator(device=dev).manual_seed(lg)
+        for lg in range(14, 25, 2):
+            nchunk = 1 << max(0, lg - top)  # chunks of the largest resident size
+            T = (1 << lg) // nchunk
+            g = torch.Generator(device=dev).manual_seed(min(lg, top))
             for op in ("hidden", "qk"):
                 if op == "hidden":
                     x = torch.randn(T, Hd, generator=g, device=dev, dtype=dt).requires_grad_(True)
@@ -577,7 +633,7 @@ def sweep(args) -> None:
                     gy = torch.randn(T, Hd, generator=g, device=dev, dtype=dt)
                     nbytes = T * (5 * Hd * s + 8)
 
-                    def step():
+                    def one():
                         return torch.autograd.grad(bloth.rms_norm(x, w, 1e-6), (x, w), gy)
                 else:
                     q = torch.randn(1, T, Hq, D, generator=g, device=dev,
@@ -590,9 +646,15 @@ def sweep(args) -> None:
                     pos = (torch.arange(T, device=dev) % 8192).view(1, T)
                     nbytes = T * ((Hq + Hk) * (5 * D * s + 8) + 16)
 
-                    def step():
+                    def one():
                         out = bloth.fused_qk_norm_rope(q, k, wq, wk, pos, inv, 1e-6)
                         return torch.autograd.grad(out, (q, k, wq, wk), (gq, gk))
+
+                def step():
+                    for _ in range(nchunk):
+                        one()
+                nbytes *= nchunk
+                unroll = 10 if nchunk == 1 else 1
                 side = torch.cuda.Stream(dev)
                 side.wait_stream(torch.cuda.current_stream(dev))
                 with torch.cuda.stream(side):
@@ -601,7 +663,7 @@ def sweep(args) -> None:
                 torch.cuda.current_stream(dev).wait_stream(side)
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(graph):
-                    for _ in range(10):
+                    for _ in range(unroll):
                         step()
                 graph.replay()
                 torch.cuda.synchronize(dev)
@@ -612,12 +674,13 @@ def sweep(args) -> None:
                     graph.replay()
                 e1.record()
                 torch.cuda.synchronize(dev)
-                ms = e0.elapsed_time(e1) / (10 * reps)
+                ms = e0.elapsed_time(e1) / (unroll * reps)
                 gbps = nbytes / (ms / 1e3) / 1e9
-                points.append({"tokens": T, "dtype": str(dt).replace("torch.", ""), "op": op,
-                               "ms_fwd_bwd": round(ms, 4), "gbps": round(gbps, 1),
-                               "frac_of_measured": round(gbps / peak, 4),
-                               "tokens_per_s": round(T / (ms / 1e3))})
+                total = T * nchunk
+                points.append({"tokens": total, "dtype": str(dt).replace("torch.", ""), "op": op,
+                               "chunks": nchunk, "ms_fwd_bwd": round(ms, 4),
+                               "gbps": round(gbps, 1), "frac_of_measured": round(gbps / peak, 4),
+                               "tokens_per_s": round(total / (ms / 1e3))})
                 del graph
                 if op == "hidden":
                     del x, w, gy
@@ -726,7 +789,8 @@ def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
     are pipelined as a streaming user would: step i+1's inputs upload on a
     copy stream while step i computes, and step i's results download on a
     third stream (two device input buffers; events order every reuse)."""
-    keys_in = [k for k in ("x", "r", "gy", "gz", "q", "k", "gq", "gk", "pos") if k in inp]
+    keys_in = [k for k in ("x", "r", "gy", "gz", "q", "k", "gq", "gk", "pos", "cos_q", "sin_q",
+                           "cos_k", "sin_k") if k in inp]
     host = {k: inp[k].detach().cpu().pin_memory() for k in keys_in}
     small = {k: v for k, v in inp.items() if k not in keys_in}
     h2d = sum(v.numel() * v.element_size() for v in host.values())

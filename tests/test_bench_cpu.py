@@ -1,0 +1,43 @@
+"""bench.py host logic on the CPU: the byte model and the synthetic inputs of
+the workloads, in particular the reference-contract one (q and k as rows with
+per-row cos/sin tables), and the CPU port that times them."""
+import math
+
+import torch
+
+import bench
+
+
+def test_rows_workload_bytes_add_the_tables_and_drop_the_positions():
+    tokens = 32768
+    pos_path = bench.step_bytes(tokens, "llama3-8b")
+    rows_path = bench.step_bytes(tokens, "llama3-8b-rows")
+    assert rows_path["rms_fwd"] == pos_path["rms_fwd"]
+    assert rows_path["rms_bwd"] == pos_path["rms_bwd"]
+    # per head row and pass: cos + sin rows of 64 bf16 = 256 B; positions 8 B per token and pass
+    heads = 32 + 8
+    assert rows_path["total"] - pos_path["total"] == tokens * (heads * 2 * 256 - 16)
+    assert rows_path["nr_fwd"] == tokens * heads * (2 * 128 * 2 + 4 + 256)
+    assert rows_path["nr_bwd"] == tokens * heads * (3 * 128 * 2 + 4 + 256)
+    assert abs(rows_path["total"] / 1e9 - 3.7017) < 1e-3
+
+
+def test_rows_workload_tables_follow_the_positions():
+    inp = bench.make_inputs("llama3-8b-rows", 1, torch.device("cpu"), seed=0)
+    S, Hq, Hk, half = 4096, 32, 8, 64
+    assert inp["cos_q"].shape == (S * Hq, half) and inp["sin_k"].shape == (S * Hk, half)
+    assert inp["cos_q"].dtype == torch.bfloat16 and inp["cos_q"].is_contiguous()
+    inv = inp["inv_freq"]
+    for s, h in ((0, 0), (7, 31), (4095, 5)):
+        ang = float(s) * inv
+        assert torch.equal(inp["cos_q"][s * Hq + h], torch.cos(ang).to(torch.bfloat16))
+        assert torch.equal(inp["sin_q"][s * Hq + h], torch.sin(ang).to(torch.bfloat16))
+        kh = h % Hk
+        assert torch.equal(inp["cos_k"][s * Hk + kh], torch.cos(ang).to(torch.bfloat16))
+    assert math.isclose(float(inv[1]), 1.0 / (5e5 ** (1 / 64)), rel_tol=1e-6)
+
+
+def test_cpu_port_runs_every_workload():
+    for name in bench.WORKLOADS:
+        bench.cpu_port_step(name, 16)()
+    assert "fused_norm_rope" in bench.describe("llama3-8b-rows")
