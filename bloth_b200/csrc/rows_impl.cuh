@@ -62,11 +62,16 @@ enum RowKind : int {
   kRowRopeVec = 3,  // kRowRope whose tables are staged in the ring and allow
                     // vector access (pipelined kernels only: neither the global
                     // table reads nor the per-element fallback are compiled)
+  kRowRopePair = 4,  // kRowRopeVec on fully rotated rows (N == 2 * half) laid out
+                     // so that a thread's second vector holds the rotation
+                     // partners of its first (TPR * VEC == half, VPT == 2)
 };
 
-constexpr bool row_rope(int kind) { return kind == kRowRope || kind == kRowRopeVec; }
+constexpr bool row_rope(int kind) {
+  return kind == kRowRope || kind == kRowRopeVec || kind == kRowRopePair;
+}
 // The kind the register kernels run for `kind` (they have one table RoPE).
-constexpr int reg_kind(int kind) { return kind == kRowRopeVec ? kRowRope : kind; }
+constexpr int reg_kind(int kind) { return row_rope(kind) ? kRowRope : kind; }
 
 // Weight of column c as the kernels apply it, w[c] + w_off, in fp32.
 __device__ __forceinline__ float ld_weight(const RowArgs& a, int64_t c) {

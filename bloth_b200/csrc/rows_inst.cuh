@@ -94,9 +94,9 @@ RowPipe pipe_plan(int N, int kind, bool bwd, bool contiguous, const RowArgs* a =
       pp.nst = nst;
     }
   }
-  // the staged-only kernel cannot run unstaged: leave those rows to the
+  // the staged-only kernels cannot run unstaged: leave those rows to the
   // register kernels
-  if (kind == kRowRopeVec && pp.cs_row_bytes == 0) pp.nst = 0;
+  if ((kind == kRowRopeVec || kind == kRowRopePair) && pp.cs_row_bytes == 0) pp.nst = 0;
   pp.ctas_per_sm = PC::BLOCK <= 128 ? pipe_ctas_per_sm(kind, bwd) : 0;
   return pp;
 }
@@ -159,6 +159,7 @@ int with_row_kind(int kind, F&& f) {
     case kRowRope: return f(std::integral_constant<int, kRowRope>{});
     case kRowRopeVec: return f(std::integral_constant<int, kRowRopeVec>{});
     case kRowAdd: return f(std::integral_constant<int, kRowAdd>{});
+    case kRowRopePair: return f(std::integral_constant<int, kRowRopePair>{});
     default: return BLOTH_ERR_ARG;
   }
 }
@@ -172,13 +173,38 @@ inline bool rows_contiguous(const RowArgs& a, int kind, bool bwd) {
   return true;
 }
 
+// Threads per row of the paired table RoPE layout for rows of 2 * half
+// (one thread per VEC columns of the first half, holding their partners of
+// the second half too), or 0 where the layout does not apply.
+template <int V>
+constexpr int pair_tpr(int64_t N, int64_t half) {
+  if (N != 2 * half || half % V != 0) return 0;
+  const int64_t t = half / V;
+  return t == 2 || t == 4 || t == 8 || t == 16 || t == 32 ? (int)t : 0;
+}
+
+// Calls f(RowCfg<TPR, 2>{}) for the paired layout's TPR.
+template <typename F>
+bool dispatch_pair_cfg(int tpr, F&& f) {
+  switch (tpr) {
+    case 2: f(RowCfg<2, 2>{}); return true;
+    case 4: f(RowCfg<4, 2>{}); return true;
+    case 8: f(RowCfg<8, 2>{}); return true;
+    case 16: f(RowCfg<16, 2>{}); return true;
+    case 32: f(RowCfg<32, 2>{}); return true;
+    default: return false;
+  }
+}
+
 // The pipelined kernels' table RoPE without the per-element fallback, when
-// the tables allow VEC-wide access everywhere.
+// the tables allow VEC-wide access everywhere and can be staged; the paired
+// layout when, in addition, the whole row is rotated.
 template <int V>
 int pipe_kind(const RowArgs& a, int kind, bool vec) {
   if (kind != kRowRope || !vec || !a.cs_vec || a.half % V != 0) return kind;
   const int es = a.cs_dt == BLOTH_F32 ? 4 : 2;  // staging needs 16-byte table rows
-  return (a.half * es) % 16 == 0 && (a.ldcs * es) % 16 == 0 ? kRowRopeVec : kind;
+  if ((a.half * es) % 16 != 0 || (a.ldcs * es) % 16 != 0) return kind;
+  return pair_tpr<V>(a.N, a.half) ? kRowRopePair : kRowRopeVec;
 }
 
 template <typename T>
@@ -189,13 +215,15 @@ int rows_fwd(const RowArgs& a, int kind, bool vec, cudaStream_t st) {
     constexpr int K = decltype(kc)::value;
     int rc = BLOTH_ERR_SHAPE;
     if (vec) {
-      dispatch_row_cfg<V>(a.N, [&](auto cfg) {
+      auto run = [&](auto cfg) {
         using C = decltype(cfg);
         using PC = PipeCfg<C::TPR, C::VPT>;
         const RowPipe pp = pipe_plan<T, PC>(a.N, K, false, rows_contiguous(a, K, false), &a);
         rc = pp.nst > 0 ? launch_row_pipe_fwd<T, V, PC, K>(a, pp, st)
                         : launch_row_fwd<T, V, C, reg_kind(K)>(a, st);
-      });
+      };
+      if constexpr (K == kRowRopePair) dispatch_pair_cfg(pair_tpr<V>(a.N, a.half), run);
+      else dispatch_row_cfg<V>(a.N, run);
     } else {
       dispatch_row_cfg<1>(a.N, [&](auto cfg) {
         rc = launch_row_fwd<T, 1, decltype(cfg), reg_kind(K)>(a, st);
@@ -216,13 +244,15 @@ int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, vo
     constexpr int K = decltype(kc)::value;
     int rc = BLOTH_ERR_SHAPE;
     if (vec) {
-      dispatch_row_cfg<V>(a.N, [&](auto cfg) {
+      auto run = [&](auto cfg) {
         using C = decltype(cfg);
         using PC = PipeCfg<C::TPR, C::VPT>;
         const RowPipe pp = pipe_plan<T, PC>(a.N, K, true, rows_contiguous(a, K, true), &a);
         rc = pp.nst > 0 ? launch_row_pipe_bwd<T, V, PC, K>(a, pp, ws, ws_bytes, dw, st)
                         : launch_row_bwd<T, V, C, reg_kind(K)>(a, ws, ws_bytes, dw, st);
-      });
+      };
+      if constexpr (K == kRowRopePair) dispatch_pair_cfg(pair_tpr<V>(a.N, a.half), run);
+      else dispatch_row_cfg<V>(a.N, run);
     } else {
       dispatch_row_cfg<1>(a.N, [&](auto cfg) {
         rc = launch_row_bwd<T, 1, decltype(cfg), reg_kind(K)>(a, ws, ws_bytes, dw, st);
@@ -245,29 +275,44 @@ size_t rows_bwd_workspace(int64_t M, int N, int kind) {
   };
   auto one_kind = [&](auto kc) {
     constexpr int K = decltype(kc)::value;
-    dispatch_row_cfg<V>(N, [&](auto cfg) {
-      using C = decltype(cfg);
-      using PC = PipeCfg<C::TPR, C::VPT>;
-      take(row_bwd_grid<T, V, C, reg_kind(K)>(M));
-      if (N % V == 0) {
-        RowPipe pp = pipe_plan<T, PC>(N, K, true, true);
-        // the staged-table kernel's plan (nst 0 here, without tables) is made
-        // per call: count it too
-        if (pp.nst > 0 || K == kRowRopeVec) {
-          if (pp.nst > 0) take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
-          // two unstaged slots: the least shared memory any plan of this
-          // shape uses, so the most CTAs (staged tables may lower the count)
-          pp.nst = 2;
-          take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
+    if constexpr (K != kRowRopePair) {  // the paired layout's shapes are counted below
+      dispatch_row_cfg<V>(N, [&](auto cfg) {
+        using C = decltype(cfg);
+        using PC = PipeCfg<C::TPR, C::VPT>;
+        take(row_bwd_grid<T, V, C, reg_kind(K)>(M));
+        if (N % V == 0) {
+          RowPipe pp = pipe_plan<T, PC>(N, K, true, true);
+          // the staged-table kernel's plan (nst 0 here, without tables) is
+          // made per call: count it too
+          if (pp.nst > 0 || K == kRowRopeVec) {
+            if (pp.nst > 0) take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
+            // two unstaged slots: the least shared memory any plan of this
+            // shape uses, so the most CTAs (staged tables may lower the count)
+            pp.nst = 2;
+            take(row_pipe_grid<T, V, PC, K, true>(M, N, pp));
+          }
         }
-      }
-    });
-    dispatch_row_cfg<1>(N, [&](auto cfg) { take(row_bwd_grid<T, 1, decltype(cfg), reg_kind(K)>(M)); });
+      });
+      dispatch_row_cfg<1>(N, [&](auto cfg) {
+        take(row_bwd_grid<T, 1, decltype(cfg), reg_kind(K)>(M));
+      });
+    }
     return 0;
   };
   with_row_kind(kind, one_kind);
   if (kind == kRowAdd) with_row_kind(kRowNorm, one_kind);
   if (kind == kRowRope) with_row_kind(kRowRopeVec, one_kind);
+  // the paired layout of fully rotated rows (half = N / 2), and its fallback
+  if (kind == kRowRope && N % 2 == 0 && pair_tpr<V>(N, N / 2) != 0) {
+    dispatch_pair_cfg(pair_tpr<V>(N, N / 2), [&](auto cfg) {
+      using C = decltype(cfg);
+      using PC = PipeCfg<C::TPR, C::VPT>;
+      take(row_bwd_grid<T, V, C, kRowRope>(M));
+      RowPipe pp = pipe_plan<T, PC>(N, kRowRopePair, true, true);
+      pp.nst = 2;  // unstaged: the least shared memory, so the most CTAs
+      take(row_pipe_grid<T, V, PC, kRowRopePair, true>(M, N, pp));
+    });
+  }
   return (size_t)grid * (size_t)N * sizeof(AccT);
 }
 

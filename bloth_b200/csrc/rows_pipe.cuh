@@ -208,6 +208,7 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
 // kinds fit in 80 registers anyway, and wider rows spill under that cap),
 // else enough for 384 threads.
 constexpr int row_pipe_min_ctas(int block, int vectors_per_thread, int kind, bool bwd) {
+  if (kind == kRowRopePair && block == 256) return bwd ? 2 : 3;
   return bwd && kind == kRowRopeVec && block == 256 && vectors_per_thread == 1
              ? 3
              : (block >= 384 ? 1 : 384 / block);
@@ -217,7 +218,10 @@ template <typename T, int VEC, int TPR, int VPT, int RPC, int KIND, bool BWD>
 __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KIND, BWD))
     row_pipe_kernel(const RowArgs a, const RowPipe pp) {
   constexpr bool ROPE = row_rope(KIND);
-  constexpr bool CSV = KIND == kRowRopeVec;  // tables known to allow vector access
+  // partner of a thread's vector 0 in its vector 1 (TPR * VEC == half, VPT == 2)
+  constexpr bool PAIR = KIND == kRowRopePair;
+  static_assert(!PAIR || VPT == 2, "the paired layout holds a column and its partner");
+  constexpr bool CSV = KIND == kRowRopeVec || PAIR;  // staged tables, vector access
   constexpr bool RES = KIND == kRowAdd;
   constexpr int NTEN = row_pipe_inputs(KIND, BWD);
   using RR = RowReduce<TPR, RPC>;
@@ -239,8 +243,11 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
   // weights in registers (VPT * VEC <= 32 for every pipelined shape), and for
   // the table RoPE on narrow rows those of their rotation partners (c +- half)
   // too (wide rows load them per vector, as registers are short there).
-  constexpr bool WP_REG = ROPE && VPT * VEC <= 16;
-  constexpr bool KEEP = VPT * VEC <= 8;
+  constexpr bool WP_REG = ROPE && !PAIR && VPT * VEC <= 16;
+  // between the backward's two passes, rows of at most 8 values per thread
+  // keep dn and xhat in registers; the paired layout (16 values) keeps dn
+  constexpr bool KEEPX = VPT * VEC <= 8;
+  constexpr bool KEEP = KEEPX || PAIR;
   float wr[VPT][VEC];
   float wpr[WP_REG ? VPT : 1][VEC];
 #pragma unroll
@@ -292,9 +299,10 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
           if (pp.cs_contiguous) {
             if (threadIdx.x == 0)
               bulk_load(d, src + row0 * pp.cs_ld_bytes, (uint32_t)(nrow * pp.cs_row_bytes), bar);
-          } else if ((int)threadIdx.x < nrow) {
-            bulk_load(d + (size_t)threadIdx.x * pp.cs_row_bytes,
-                      src + (row0 + threadIdx.x) * pp.cs_ld_bytes, (uint32_t)pp.cs_row_bytes, bar);
+          } else {  // one copy per row; blocks can hold more rows than warp 0 has lanes
+            for (int r = (int)threadIdx.x; r < nrow; r += 32)
+              bulk_load(d + (size_t)r * pp.cs_row_bytes, src + (row0 + r) * pp.cs_ld_bytes,
+                        (uint32_t)pp.cs_row_bytes, bar);
           }
         }
       }
@@ -313,13 +321,15 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
           if constexpr (BWD) bulk_load(d, src + row0 * ld, (uint32_t)(nrow * pp.row_bytes), bar);
           else bulk_load_hint(d, src + row0 * ld, (uint32_t)(nrow * pp.row_bytes), bar, pol);
         }
-      } else if ((int)threadIdx.x < nrow) {
-        if constexpr (BWD)
-          bulk_load(d + (size_t)threadIdx.x * pp.row_bytes, src + (row0 + threadIdx.x) * ld,
-                    (uint32_t)pp.row_bytes, bar);
-        else
-          bulk_load_hint(d + (size_t)threadIdx.x * pp.row_bytes, src + (row0 + threadIdx.x) * ld,
-                         (uint32_t)pp.row_bytes, bar, pol);
+      } else {  // one copy per row, from the lanes of warp 0
+        for (int r = (int)threadIdx.x; r < nrow; r += 32) {
+          if constexpr (BWD)
+            bulk_load(d + (size_t)r * pp.row_bytes, src + (row0 + r) * ld, (uint32_t)pp.row_bytes,
+                      bar);
+          else
+            bulk_load_hint(d + (size_t)r * pp.row_bytes, src + (row0 + r) * ld,
+                           (uint32_t)pp.row_bytes, bar, pol);
+        }
       }
     }
   };
@@ -408,6 +418,33 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
       if (valid) {
         if (lt == 0) a.rstd_out[row] = rstd;
         T* yr = reinterpret_cast<T*>(a.out) + row * a.ldo;
+        if constexpr (PAIR) {
+          // y_c = rstd (a_c cos - a_p sin), y_p = rstd (a_p cos + a_c sin) for
+          // column c < half and its partner p = c + half, a = x w; cos and sin
+          // read once for both, the partner already in registers
+          const int c0 = lt * VEC;
+          float f0[VEC], f1[VEC], cs[VEC], sn[VEC];
+          unpack(xp[0], f0);
+          unpack(xp[1], f1);
+          lds_any_vec<VEC>(csp, c0, a.cs_dt, cs);
+          lds_any_vec<VEC>(snp, c0, a.cs_dt, sn);
+          const float2 r2 = f2s(rstd), nr2 = f2s(-rstd);
+#pragma unroll
+          for (int e = 0; e < VEC; e += 2) {
+            const float2 a0 = f2_mul(f2(f0[e], f0[e + 1]), f2(wr[0][e], wr[0][e + 1]));
+            const float2 a1 = f2_mul(f2(f1[e], f1[e + 1]), f2(wr[1][e], wr[1][e + 1]));
+            const float2 c2 = f2_mul(f2(cs[e], cs[e + 1]), r2);
+            const float2 s2 = f2(sn[e], sn[e + 1]);
+            const float2 y0 = f2_fma(a1, f2_mul(s2, nr2), f2_mul(a0, c2));
+            const float2 y1 = f2_fma(a0, f2_mul(s2, r2), f2_mul(a1, c2));
+            f0[e] = y0.x;
+            f0[e + 1] = y0.y;
+            f1[e] = y1.x;
+            f1[e + 1] = y1.y;
+          }
+          stg_pack_stream<T, VEC>(yr + c0, pack<T, VEC>(f0));
+          stg_pack_stream<T, VEC>(yr + c0 + TPR * VEC, pack<T, VEC>(f1));
+        } else {
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
           const int c = (j * TPR + lt) * VEC;
@@ -430,6 +467,7 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
             else stg_pack_stream<T, VEC>(yr + c, pack<T, VEC>(f));
           }
         }
+        }
       }
     } else {
       const unsigned char* dyp = slot + (size_t)grp * pp.row_bytes;
@@ -440,15 +478,44 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
       const float2 r2 = f2s(rstd);
       // narrow rows keep dn and xhat in registers for pass 2 (instead of
       // re-reading the slot and, for RoPE, rotating dy again)
-      float dnk[KEEP ? VPT : 1][VEC], xk[KEEP ? VPT : 1][VEC];
+      float dnk[KEEP ? VPT : 1][VEC], xk[KEEPX ? VPT : 1][VEC];
+      // paired layout: dn = R^T dy of both vectors at once,
+      //   dn_c = dy_c cos + dy_p sin,  dn_p = dy_p cos - dy_c sin
+      float dpr[PAIR ? 2 : 1][VEC];
+      if constexpr (PAIR) {
+        if (valid) {
+          const int c0 = lt * VEC;
+          float g0[VEC], g1[VEC], cs[VEC], sn[VEC];
+          unpack(lds_pack<T, VEC>(dyp + (int64_t)c0 * sizeof(T)), g0);
+          unpack(lds_pack<T, VEC>(dyp + (int64_t)(c0 + TPR * VEC) * sizeof(T)), g1);
+          lds_any_vec<VEC>(csp, c0, a.cs_dt, cs);
+          lds_any_vec<VEC>(snp, c0, a.cs_dt, sn);
+#pragma unroll
+          for (int e = 0; e < VEC; e += 2) {
+            const float2 c2 = f2(cs[e], cs[e + 1]), s2 = f2(sn[e], sn[e + 1]);
+            const float2 d0 = f2(g0[e], g0[e + 1]), d1 = f2(g1[e], g1[e + 1]);
+            const float2 n0 = f2_fma(d1, s2, f2_mul(d0, c2));
+            const float2 n1 = f2_fma(d0, f2_mul(s2, f2s(-1.f)), f2_mul(d1, c2));
+            dpr[0][e] = n0.x;
+            dpr[0][e + 1] = n0.y;
+            dpr[PAIR ? 1 : 0][e] = n1.x;
+            dpr[PAIR ? 1 : 0][e + 1] = n1.y;
+          }
+        }
+      }
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int c = (j * TPR + lt) * VEC;
         if (valid && c < N) {
           float xf[VEC], dn[VEC];
-          unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
+          if constexpr (PAIR) {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) dn[e] = dpr[PAIR ? j : 0][e];
+          } else {
+            unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
+          }
           unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
-          if constexpr (ROPE) rope_pipe_bwd<T, VEC, CSV>(dn, c, dyp, a, row, csp, snp);
+          if constexpr (ROPE && !PAIR) rope_pipe_bwd<T, VEC, CSV>(dn, c, dyp, a, row, csp, snp);
 #pragma unroll
           for (int e = 0; e < VEC; e += 2) {
             const float2 d2 = f2(dn[e], dn[e + 1]);
@@ -456,8 +523,10 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
             if constexpr (KEEP) {
               dnk[KEEP ? j : 0][e] = d2.x;
               dnk[KEEP ? j : 0][e + 1] = d2.y;
-              xk[KEEP ? j : 0][e] = x2.x;
-              xk[KEEP ? j : 0][e + 1] = x2.y;
+            }
+            if constexpr (KEEPX) {
+              xk[KEEPX ? j : 0][e] = x2.x;
+              xk[KEEPX ? j : 0][e + 1] = x2.y;
             }
             const float2 t = f2_mul(d2, f2(wr[j][e], wr[j][e + 1]));
             if ((e / 2) & 1) db = f2_fma(t, x2, db);
@@ -484,9 +553,12 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
             float xf[VEC], dn[VEC], o[VEC];
             if constexpr (KEEP) {
 #pragma unroll
-              for (int e = 0; e < VEC; ++e) {
-                dn[e] = dnk[KEEP ? j : 0][e];
-                xf[e] = xk[KEEP ? j : 0][e];
+              for (int e = 0; e < VEC; ++e) dn[e] = dnk[KEEP ? j : 0][e];
+              if constexpr (KEEPX) {
+#pragma unroll
+                for (int e = 0; e < VEC; ++e) xf[e] = xk[KEEPX ? j : 0][e];
+              } else {
+                unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);
               }
             } else {
               unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
@@ -497,7 +569,7 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
 #pragma unroll
             for (int e = 0; e < VEC; e += 2) {
               // xf holds xhat already when kept
-              const float2 x2 = KEEP ? f2(xf[e], xf[e + 1]) : f2_mul(f2(xf[e], xf[e + 1]), r2);
+              const float2 x2 = KEEPX ? f2(xf[e], xf[e + 1]) : f2_mul(f2(xf[e], xf[e + 1]), r2);
               const float2 y = f2_mul(
                   f2_fma(x2, nd, f2_mul(f2(dn[e], dn[e + 1]), f2(wr[j][e], wr[j][e + 1]))), r2);
               o[e] = y.x;
@@ -525,30 +597,28 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
   }
 
   if constexpr (BWD) {
-    // Fold the RPC row groups' accumulators into group 0 in a fixed order
-    // through the idle ring memory, then write this CTA's partial row.
+    // This CTA's partial dweight row: the RPC row groups' accumulators are
+    // stored side by side in the idle ring memory ([RPC][N], which always
+    // fits: the ring holds at least two slots of two input rows per group),
+    // then each thread sums columns over the groups in a fixed order.
     __syncthreads();
+    AccT* part = reinterpret_cast<AccT*>(a.partials) + (int64_t)blockIdx.x * N;
     if constexpr (RPC > 1) {
       AccT* buf = reinterpret_cast<AccT*>(smem);
-      for (int g = RPC - 1; g >= 1; --g) {
-        if (grp == g) {
 #pragma unroll
-          for (int j = 0; j < VPT; ++j)
+      for (int j = 0; j < VPT; ++j) {
+        const int c = (j * TPR + lt) * VEC;
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) buf[(j * TPR + lt) * VEC + e] = acc[j][e];
-        }
-        __syncthreads();
-        if (grp == 0) {
-#pragma unroll
-          for (int j = 0; j < VPT; ++j)
-#pragma unroll
-            for (int e = 0; e < VEC; ++e) acc[j][e] += buf[(j * TPR + lt) * VEC + e];
-        }
-        __syncthreads();
+        for (int e = 0; e < VEC; ++e)
+          if (c + e < N) buf[grp * N + c + e] = acc[j][e];
       }
-    }
-    if (grp == 0) {
-      AccT* part = reinterpret_cast<AccT*>(a.partials) + (int64_t)blockIdx.x * N;
+      __syncthreads();
+      for (int col = (int)threadIdx.x; col < N; col += TPR * RPC) {
+        AccT sum = buf[col];
+        for (int g = 1; g < RPC; ++g) sum += buf[g * N + col];
+        part[col] = sum;
+      }
+    } else {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int c = (j * TPR + lt) * VEC;

@@ -10,7 +10,10 @@ up to 32 rows each) through the library's own workspace query and check the
 results against the oracle, evaluated in float64 on the GPU. The table cases
 cover cos/sin rows that are staged in one copy per block (contiguous), one
 copy per row (strided, 16-byte aligned) and read from global memory
-(strided, misaligned). Tolerances are the path's (see oracle.tolerance_ok).
+(strided, misaligned). Staged tables on fully rotated rows take the paired
+layout (a thread holds a column and its rotation partner), with 2 to 32
+threads per row over these widths. Tolerances are the path's (see
+oracle.tolerance_ok).
 """
 import pytest
 import torch
@@ -36,7 +39,7 @@ def _rows(N):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("N", [64, 128, 256, 512])
+@pytest.mark.parametrize("N", [32, 64, 128, 256, 512])
 @pytest.mark.parametrize("layout", ["contiguous", "strided", "misaligned"])
 def test_table_rope_backward_full_wave(cuda, dtype, N, layout):
     M, h, eps = _rows(N), N // 2, 1e-6
