@@ -44,8 +44,8 @@ PROFILED_TRAFFIC = {
     ("llama3-8b", "bloth_rmsnorm_fwd"): 268_540_416 + 214_617_600,
     ("llama3-8b", "bloth_rmsnorm_bwd"): 537_134_848 + 238_408_704,
     # reference-contract rows: the q and the k launch of the call together
-    ("llama3-8b-rows", "bloth_norm_rope_fwd"): 536_903_680 + 225_532_416 + 134_250_752 + 22_435_584,
-    ("llama3-8b-rows", "bloth_norm_rope_bwd"): 809_702_400 + 246_857_728 + 202_416_640 + 45_428_992,
+    ("llama3-8b-rows", "bloth_norm_rope_fwd"): 536_898_304 + 225_586_688 + 134_242_304 + 19_341_312,
+    ("llama3-8b-rows", "bloth_norm_rope_bwd"): 809_533_696 + 245_780_992 + 202_408_960 + 45_013_504,
 }
 NOMINAL_HBM_GBS = 8000.0
 
