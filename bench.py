@@ -44,8 +44,8 @@ PROFILED_TRAFFIC = {
     ("llama3-8b", "bloth_rmsnorm_fwd"): 268_540_416 + 214_617_600,
     ("llama3-8b", "bloth_rmsnorm_bwd"): 537_134_848 + 238_408_704,
     # reference-contract rows: the q and the k launch of the call together
-    ("llama3-8b-rows", "bloth_norm_rope_fwd"): 536_898_304 + 225_586_688 + 134_242_304 + 19_341_312,
-    ("llama3-8b-rows", "bloth_norm_rope_bwd"): 809_533_696 + 245_780_992 + 202_408_960 + 45_013_504,
+    ("llama3-8b-rows", "bloth_norm_rope_fwd"): 536_897_280 + 224_008_704 + 134_242_304 + 20_562_944,
+    ("llama3-8b-rows", "bloth_norm_rope_bwd"): 809_656_576 + 244_946_432 + 202_408_960 + 42_970_112,
 }
 NOMINAL_HBM_GBS = 8000.0
 

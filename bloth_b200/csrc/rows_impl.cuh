@@ -398,11 +398,13 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_ke
 // ---------------------------------------------------------------------------
 // launch configuration
 // ---------------------------------------------------------------------------
-template <int TPR_, int VPT_>
+template <int TPR_, int VPT_, int PIPE_BLOCK_ = 0>
 struct RowCfg {
   static constexpr int TPR = TPR_;
   static constexpr int VPT = VPT_;
   static constexpr int RPC = TPR >= 256 ? 1 : 256 / TPR;
+  // threads per CTA of the pipelined kernel for this shape (0: PipeCfg's rule)
+  static constexpr int PIPE_BLOCK = PIPE_BLOCK_;
 };
 
 // Picks the smallest row-group shape that holds a row of N in registers and

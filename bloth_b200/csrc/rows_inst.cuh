@@ -97,7 +97,9 @@ RowPipe pipe_plan(int N, int kind, bool bwd, bool contiguous, const RowArgs* a =
   // the staged-only kernels cannot run unstaged: leave those rows to the
   // register kernels
   if ((kind == kRowRopeVec || kind == kRowRopePair) && pp.cs_row_bytes == 0) pp.nst = 0;
-  pp.ctas_per_sm = PC::BLOCK <= 128 ? pipe_ctas_per_sm(kind, bwd) : 0;
+  // (the per-kind caps were measured for wide rows; the paired table layout
+  // runs as many CTAs as fit)
+  pp.ctas_per_sm = PC::BLOCK <= 128 && kind != kRowRopePair ? pipe_ctas_per_sm(kind, bwd) : 0;
   return pp;
 }
 
@@ -183,15 +185,19 @@ constexpr int pair_tpr(int64_t N, int64_t half) {
   return t == 2 || t == 4 || t == 8 || t == 16 || t == 32 ? (int)t : 0;
 }
 
-// Calls f(RowCfg<TPR, 2>{}) for the paired layout's TPR.
+// Calls f(RowCfg<TPR, 2, 128>{}) for the paired layout's TPR. Its pipelined
+// kernels run 128-thread CTAs: the backward (112-125 registers) then fits
+// 4 CTAs, 16 warps, per SM with half as many warps per block barrier as
+// 2 CTAs of 256 threads (measured at 2^20 rows of 128 bf16: backward 179.1 vs
+// 191.5 us, forward 129.1 us either way).
 template <typename F>
 bool dispatch_pair_cfg(int tpr, F&& f) {
   switch (tpr) {
-    case 2: f(RowCfg<2, 2>{}); return true;
-    case 4: f(RowCfg<4, 2>{}); return true;
-    case 8: f(RowCfg<8, 2>{}); return true;
-    case 16: f(RowCfg<16, 2>{}); return true;
-    case 32: f(RowCfg<32, 2>{}); return true;
+    case 2: f(RowCfg<2, 2, 128>{}); return true;
+    case 4: f(RowCfg<4, 2, 128>{}); return true;
+    case 8: f(RowCfg<8, 2, 128>{}); return true;
+    case 16: f(RowCfg<16, 2, 128>{}); return true;
+    case 32: f(RowCfg<32, 2, 128>{}); return true;
     default: return false;
   }
 }
@@ -217,7 +223,7 @@ int rows_fwd(const RowArgs& a, int kind, bool vec, cudaStream_t st) {
     if (vec) {
       auto run = [&](auto cfg) {
         using C = decltype(cfg);
-        using PC = PipeCfg<C::TPR, C::VPT>;
+        using PC = PipeCfg<C::TPR, C::VPT, C::PIPE_BLOCK>;
         const RowPipe pp = pipe_plan<T, PC>(a.N, K, false, rows_contiguous(a, K, false), &a);
         rc = pp.nst > 0 ? launch_row_pipe_fwd<T, V, PC, K>(a, pp, st)
                         : launch_row_fwd<T, V, C, reg_kind(K)>(a, st);
@@ -246,7 +252,7 @@ int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, vo
     if (vec) {
       auto run = [&](auto cfg) {
         using C = decltype(cfg);
-        using PC = PipeCfg<C::TPR, C::VPT>;
+        using PC = PipeCfg<C::TPR, C::VPT, C::PIPE_BLOCK>;
         const RowPipe pp = pipe_plan<T, PC>(a.N, K, true, rows_contiguous(a, K, true), &a);
         rc = pp.nst > 0 ? launch_row_pipe_bwd<T, V, PC, K>(a, pp, ws, ws_bytes, dw, st)
                         : launch_row_bwd<T, V, C, reg_kind(K)>(a, ws, ws_bytes, dw, st);
@@ -278,7 +284,7 @@ size_t rows_bwd_workspace(int64_t M, int N, int kind) {
     if constexpr (K != kRowRopePair) {  // the paired layout's shapes are counted below
       dispatch_row_cfg<V>(N, [&](auto cfg) {
         using C = decltype(cfg);
-        using PC = PipeCfg<C::TPR, C::VPT>;
+        using PC = PipeCfg<C::TPR, C::VPT, C::PIPE_BLOCK>;
         take(row_bwd_grid<T, V, C, reg_kind(K)>(M));
         if (N % V == 0) {
           RowPipe pp = pipe_plan<T, PC>(N, K, true, true);
@@ -306,7 +312,7 @@ size_t rows_bwd_workspace(int64_t M, int N, int kind) {
   if (kind == kRowRope && N % 2 == 0 && pair_tpr<V>(N, N / 2) != 0) {
     dispatch_pair_cfg(pair_tpr<V>(N, N / 2), [&](auto cfg) {
       using C = decltype(cfg);
-      using PC = PipeCfg<C::TPR, C::VPT>;
+      using PC = PipeCfg<C::TPR, C::VPT, C::PIPE_BLOCK>;
       take(row_bwd_grid<T, V, C, kRowRope>(M));
       RowPipe pp = pipe_plan<T, PC>(N, kRowRopePair, true, true);
       pp.nst = 2;  // unstaged: the least shared memory, so the most CTAs

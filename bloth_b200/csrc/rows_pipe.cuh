@@ -80,15 +80,17 @@ constexpr int row_pipe_inputs(int kind, bool bwd) {
 // thread as the register kernels, but RPC = 128 / TPR rows per block (one
 // row for wide rows), so a CTA is 128 threads or one row group, and several
 // CTAs share an SM.
-template <int TPR_, int VPT_>
+template <int TPR_, int VPT_, int BLOCK_ = 0>
 struct PipeCfg {
   static constexpr int TPR = TPR_;
   static constexpr int VPT = VPT_;
   // Narrow rows (at most 64 vectors, e.g. bf16 head rows of 128-512) get
   // 256-thread CTAs, so that a block of rows (4-8 KB) amortises the per-block
   // wait and barrier: 1.4-1.6x faster than 128 threads at rows of 128-512.
+  // BLOCK_ > 0 fixes the CTA size instead (the paired table RoPE layout).
   static constexpr bool NARROW = TPR * VPT <= 64;
-  static constexpr int RPC = TPR >= 128 ? 1 : (NARROW ? 256 : 128) / TPR;
+  static constexpr int RPC =
+      BLOCK_ > 0 ? BLOCK_ / TPR : (TPR >= 128 ? 1 : (NARROW ? 256 : 128) / TPR);
   static constexpr int BLOCK = TPR * RPC;
   static constexpr int MIN_BLOCKS = BLOCK >= 512 ? 1 : 512 / BLOCK;
 };
@@ -208,7 +210,6 @@ __device__ __forceinline__ void rope_pipe_bwd(float (&d)[VEC], int c, const unsi
 // kinds fit in 80 registers anyway, and wider rows spill under that cap),
 // else enough for 384 threads.
 constexpr int row_pipe_min_ctas(int block, int vectors_per_thread, int kind, bool bwd) {
-  if (kind == kRowRopePair && block == 256) return bwd ? 2 : 3;
   return bwd && kind == kRowRopeVec && block == 256 && vectors_per_thread == 1
              ? 3
              : (block >= 384 ? 1 : 384 / block);
