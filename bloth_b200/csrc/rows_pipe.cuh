@@ -9,12 +9,14 @@
 // waits for block i, so NST - 1 blocks are in flight while one is computed.
 // A slot holds the block's rows of each input tensor, one after another:
 // x (forward), dy then x (backward), and for the residual add x then r
-// (forward) or dy, z then dz_out (backward). NST and the slot size are chosen
-// on the host from N so that a CTA uses at most ~200 KB of shared memory. The
-// trailing __syncthreads of an iteration releases its slot.
+// (forward) or dy, z then dz_out (backward), then, for the table RoPE, the
+// rows' cos and sin. NST and the slot size are chosen on the host from N so
+// that a CTA stays within its shared-memory budget. The trailing
+// __syncthreads of an iteration releases its slot.
 //
 // Math: as rows_impl.cuh (reference bloth/bloth/kernels/rms_norm.py:59-111,
-// fused_norm_qkv_rope.py:59-96); the RoPE partner half is read from the
+// fused_norm_qkv_rope.py:59-96). The table RoPE's partner half is either in
+// the thread's other vector (paired layout, kRowRopePair) or read from the
 // staged row in shared memory.
 #pragma once
 
@@ -77,9 +79,9 @@ constexpr int row_pipe_inputs(int kind, bool bwd) {
 }
 
 // CTA shape of the pipelined kernels: TPR threads per row and VPT vectors per
-// thread as the register kernels, but RPC = 128 / TPR rows per block (one
-// row for wide rows), so a CTA is 128 threads or one row group, and several
-// CTAs share an SM.
+// thread as the register kernels, with RPC rows per block: one row for wide
+// rows (TPR >= 128), 128-thread CTAs for medium rows, 256-thread CTAs for
+// narrow ones, or a fixed CTA size. Several CTAs share an SM.
 template <int TPR_, int VPT_, int BLOCK_ = 0>
 struct PipeCfg {
   static constexpr int TPR = TPR_;
