@@ -435,6 +435,34 @@ def test_table_variant_edge_cases(cuda):
     assert mod(x.detach().view(3, 11, N), cos.to(cuda), sin.to(cuda)).shape == (3, 11, N)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("N", [32, 64, 128, 256])
+def test_paired_table_rows_with_strided_inputs(cuda, dtype, N):
+    # Fully rotated rows with staged tables take the paired layout (a thread
+    # holds a column and its rotation partner), 4-64 rows per block at these
+    # widths. Strided x and dy rows are bulk-copied one row at a time, and
+    # 1001 rows leave a partial last block. The weight is applied as w + 1.
+    from bloth_b200.kernels.fused_norm_qkv_rope import norm_rope_backward, norm_rope_forward
+    M, h, eps, off = 1001, N // 2, 1e-6, 1.0
+    x = seeded_normal((M, N + 8), dtype, 40).to(cuda)[:, :N]
+    dy = seeded_normal((M, N + 8), dtype, 41).to(cuda)[:, :N]
+    w = (seeded_weight(N, torch.float32, 42) - 1.0).to(dtype).to(cuda)
+    ang = seeded_normal((M, h), torch.float32, 43) * 3.0
+    cs_dtype = torch.float32 if dtype == torch.float32 else dtype
+    cos, sin = ang.cos().to(cs_dtype).to(cuda), ang.sin().to(cs_dtype).to(cuda)
+    assert x.stride(0) == N + 8 and dy.stride(0) == N + 8
+    y, rstd = norm_rope_forward(x, w, cos, sin, eps, off)
+    dx, dw = norm_rope_backward(dy, x, w, cos, sin, rstd, off)
+    xc, dyc, cc, sc = x.cpu(), dy.cpu(), cos.cpu(), sin.cpu()
+    weff = w.cpu().to(F64) + off
+    ry, _, rdx, rdw = oracle.norm_rope_table_fwd_bwd(xc, weff, cc, sc, dyc, eps)
+    assert_tol(y.cpu(), ry, dtype, "paired y")
+    assert_tol(dx.cpu(), rdx, dtype, "paired dx")
+    assert_tol(dw.cpu(), rdw, dtype, "paired dw", True,
+               oracle.norm_rope_table_dw_scale(xc, cc, sc, dyc, eps))
+    assert bloth_b200._lib.load().bloth_device_fault(0) == 0
+
+
 def test_rope_only_autograd(cuda):
     for dtype in (torch.float32, torch.bfloat16):
         x = seeded_normal((2, 40, 6, 128), dtype, 30).to(cuda).requires_grad_(True)
