@@ -7,15 +7,32 @@ in-register), then the backward of both for given output gradients (dx,
 dweight, dq, dk, dwq, dwk) via ``torch.autograd.grad``.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
-                    [--impl b200|reference] [--scaling weak|strong]
+                    [--impl b200|reference|reference-triton]
+                    [--scaling weak|strong] [--shard-of N]
 
 N > 1 is launched with torch.distributed.run, one rank per GPU; every rank
-processes its own shard of token rows (no collective on the data path); the
-step time is the max over ranks. Prints one JSON line on rank 0.
+processes its own contiguous shard of batch rows (no collective on the data
+path); the step time is the max over ranks. Prints one JSON line on rank 0.
+
+Scaling. The Llama-3-8B and the Qwen3-8B packed workloads are defined as one
+batch whose token rows are sharded over the GPUs, so they default to strong
+scaling: at N GPUs each rank takes batch/N rows (Llama-3-8B: 32768 tokens on
+one GPU, 4096 per GPU on eight). The other workloads default to weak scaling
+(the full batch on every rank). ``--shard-of N`` runs, on one GPU, the shard
+that rank 0 of an N-rank strong-scaling job processes.
+
+Checks. After the timed region every rank reads the library's device fault
+word and re-runs one step whose results are checked: sampled tokens of the
+rank's shard against the CPU oracle, and the weight gradients summed over the
+ranks (one all-reduce, outside the timed region) against the float64 oracle
+over the whole batch and, at N > 1, against the same kernels run over the
+whole batch on one GPU. The line carries ``fault`` and ``parity_ok``.
 
 ``--impl reference`` times the reference's CPU path instead: the oracle's
-PyTorch restatement in float32 on all host cores, on a bounded sample of the
+PyTorch restatement in float32 on all host cores, on a fixed sample of the
 same workload per step (the reference has no CPU implementation of its own).
+``--impl reference-triton`` times the reference's own Triton kernels from the
+package installed under baseline/_ref (one GPU).
 """
 from __future__ import annotations
 
@@ -25,6 +42,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -66,6 +84,13 @@ WORKLOADS = {
 }
 RESIDUAL = {"llama3-8b-residual"}
 ROWS = {"llama3-8b-rows"}
+# workloads defined as one batch whose token rows are sharded over the GPUs
+SHARDED = {"llama3-8b", "qwen3-8b-packed"}
+
+# tokens per step of the CPU timings (the reference arm and the GPU arm's
+# cpu_baseline leg time the same sample), and their minimum duration
+CPU_SAMPLE_TOKENS = 512
+CPU_MIN_SECONDS = 12.0
 
 
 def describe(name: str) -> str:
@@ -118,6 +143,12 @@ def step_bytes(tokens: int, name: str, elem: int = 2) -> dict:
 
 
 # ------------------------------------------------------------- ranks
+def default_scaling(name: str) -> str:
+    """Strong scaling (the batch's rows split over the ranks) for the
+    workloads defined as one sharded batch, weak scaling otherwise."""
+    return "strong" if name in SHARDED else "weak"
+
+
 def local_batch(batch: int, world: int, scaling: str) -> int:
     """Batch rows (sequences) one rank processes: the full batch per rank
     under weak scaling, an equal share of it under strong scaling."""
@@ -126,6 +157,15 @@ def local_batch(batch: int, world: int, scaling: str) -> int:
     if batch % world:
         raise ValueError(f"strong scaling needs batch {batch} divisible by {world} ranks")
     return batch // world
+
+
+def shard_rows(batch: int, world: int, rank: int, scaling: str) -> range:
+    """Global batch-row indices of `rank`'s shard: a contiguous block of
+    batch/world rows under strong scaling; under weak scaling every rank
+    takes a full batch of its own (rows rank*batch ...), so that the inputs of
+    different ranks differ."""
+    b = local_batch(batch, world, scaling)
+    return range(rank * b, (rank + 1) * b)
 
 
 def max_over_ranks(value: float, dist, device) -> float:
@@ -140,36 +180,50 @@ def max_over_ranks(value: float, dist, device) -> float:
 
 
 # ------------------------------------------------------------- inputs
-def make_inputs(name: str, tokens_b: int, dev, seed: int, shard=(0, 1)):
-    """Seeded synthetic inputs on `dev` for batch rows shard[0]::shard[1]."""
-    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
-    g = torch.Generator(device=dev).manual_seed(seed)
-    bf = torch.bfloat16
+def _row_seed(seed: int, row: int) -> int:
+    return seed * 100003 + 7919 * (row + 1)
 
-    def randn(*shape):
-        return torch.randn(*shape, generator=g, device=dev, dtype=torch.float32).to(bf)
+
+def make_inputs(name: str, rows, dev, seed: int = 1234):
+    """Seeded synthetic inputs on `dev` for the batch rows `rows` (a range of
+    global batch-row indices, or a count meaning range(count)).
+
+    Every batch row (sequence) is drawn from its own generator seeded by
+    (seed, row), so a rank's shard holds exactly the rows of the whole batch
+    it covers, wherever it is generated. Weights depend on `seed` only (they
+    are replicated on every rank)."""
+    if isinstance(rows, int):
+        rows = range(rows)
+    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+    bf = torch.bfloat16
+    b = len(rows)
+    wg = torch.Generator(device=dev).manual_seed(seed)
 
     def weight(n):
-        return (1 + 0.1 * torch.randn(n, generator=g, device=dev)).to(bf)
+        return (1 + 0.1 * torch.randn(n, generator=wg, device=dev)).to(bf)
 
-    b = tokens_b
-    inp = {}
+    shapes = {}
     if Hd:
-        inp["x"] = randn(b, S, Hd)
-        inp["w"] = weight(Hd)
-        inp["gy"] = randn(b, S, Hd)
+        shapes["x"] = (S, Hd)
+        shapes["gy"] = (S, Hd)
         if name in RESIDUAL:
-            inp["r"] = randn(b, S, Hd)
-            inp["gz"] = randn(b, S, Hd)
-    inp["q"] = randn(b, S, Hq, D)
-    inp["k"] = randn(b, S, Hk, D)
+            shapes["r"] = (S, Hd)
+            shapes["gz"] = (S, Hd)
+    shapes.update(q=(S, Hq, D), k=(S, Hk, D), gq=(S, Hq, D), gk=(S, Hk, D))
+    inp = {key: torch.empty((b, *shp), dtype=bf, device=dev) for key, shp in shapes.items()}
+    for i, r in enumerate(rows):
+        g = torch.Generator(device=dev).manual_seed(_row_seed(seed, r))
+        for key, shp in shapes.items():
+            inp[key][i].copy_(torch.randn(*shp, generator=g, device=dev, dtype=torch.float32))
+    if Hd:
+        inp["w"] = weight(Hd)
     inp["wq"] = weight(D)
     inp["wk"] = weight(D)
-    inp["gq"] = randn(b, S, Hq, D)
-    inp["gk"] = randn(b, S, Hk, D)
     if packed:
         from oracle.reference_path import packed_position_ids  # seeded document layout
-        pos = packed_position_ids(b, S, 64, 2048, torch.Generator().manual_seed(seed + shard[0]))
+        pos = torch.cat([packed_position_ids(1, S, 64, 2048,
+                                             torch.Generator().manual_seed(_row_seed(seed, r)))
+                         for r in rows]) if b else torch.empty(0, S, dtype=torch.int64)
         inp["pos"] = pos.to(dev)
     else:
         inp["pos"] = torch.arange(S, device=dev, dtype=torch.int64).expand(b, S).contiguous()
@@ -188,23 +242,22 @@ def make_inputs(name: str, tokens_b: int, dev, seed: int, shard=(0, 1)):
 
 
 def run_step(inp, bloth):
-    """One fwd+bwd pass through the public API; returns the gradients."""
-    leaves = []
-    outs, grads = [], []
+    """One fwd+bwd pass through the public API; returns (outputs, gradients)
+    as dicts keyed by name."""
+    leaves, outs, grads = {}, {}, []
     if "r" in inp:
         x = inp["x"].requires_grad_(True)
         r = inp["r"].requires_grad_(True)
         w = inp["w"].requires_grad_(True)
-        y, z = bloth.fused_add_rms_norm(x, r, w, inp["eps"])
-        outs += [y, z]
+        outs["y"], outs["z"] = bloth.fused_add_rms_norm(x, r, w, inp["eps"])
         grads += [inp["gy"], inp["gz"]]
-        leaves += [x, r, w]
+        leaves.update(dx=x, dr=r, dw=w)
     elif "x" in inp:
         x = inp["x"].requires_grad_(True)
         w = inp["w"].requires_grad_(True)
-        outs.append(bloth.rms_norm(x, w, inp["eps"]))
+        outs["y"] = bloth.rms_norm(x, w, inp["eps"])
         grads.append(inp["gy"])
-        leaves += [x, w]
+        leaves.update(dx=x, dw=w)
     q = inp["q"].requires_grad_(True)
     k = inp["k"].requires_grad_(True)
     wq = inp["wq"].requires_grad_(True)
@@ -214,16 +267,141 @@ def run_step(inp, bloth):
         ko = bloth.kernels.fused_norm_rope(k, wk, inp["cos_k"], inp["sin_k"], inp["eps"])
     else:
         qo, ko = bloth.fused_qk_norm_rope(q, k, wq, wk, inp["pos"], inp["inv_freq"], inp["eps"])
-    outs += [qo, ko]
+    outs.update(q_out=qo, k_out=ko)
     grads += [inp["gq"], inp["gk"]]
-    leaves += [q, k, wq, wk]
-    res = torch.autograd.grad(outs, leaves, grads)
-    return outs, res
+    leaves.update(dq=q, dk=k, dwq=wq, dwk=wk)
+    res = torch.autograd.grad(list(outs.values()), list(leaves.values()), grads)
+    return outs, dict(zip(leaves, res))
+
+
+# ------------------------------------------------------------- checks
+def check_step(name: str, inp, bloth, dev, dist, world: int, rank: int, rows: range,
+               seed: int, n_sample: int = 64) -> dict:
+    """Checks one step of this rank's shard, outside any timed region.
+
+    Tokens are independent, so `n_sample` sampled tokens of the shard are
+    checked against the CPU oracle (float64) at the path's tolerance (bf16:
+    abs <= 2e-2 or rel <= 1.6e-2). Weight gradients sum over every token of
+    the batch: each rank's dweight (in the weight's dtype) is summed over the
+    ranks by one all-reduce, and rank 0 compares the sum with the float64
+    oracle over the whole batch and, at N > 1, with the same kernels run over
+    the whole batch on its GPU. Each rank's dweight is rounded to bf16 before
+    the sum, so the bound on the sum is the bf16 rule applied to the sum of
+    the parts' magnitudes. Returns the check's record (rank 0's view)."""
+    import oracle
+    from oracle.reference_path import tolerance_ok
+    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+    bf = torch.bfloat16
+    outs, grads = run_step(inp, bloth)
+    torch.cuda.synchronize(dev)
+    worst = 0.0
+    ok = True
+
+    def note(good, excess):
+        nonlocal ok, worst
+        ok = ok and bool(good)
+        worst = max(worst, float(excess))
+
+    # ---- sampled tokens against the CPU oracle
+    b = len(rows)
+    gen = torch.Generator().manual_seed(97 + rank)
+    flat = torch.randperm(b * S, generator=gen)[:n_sample]
+    bi, si = flat // S, flat % S
+    sel = lambda t: t.detach()[bi.to(t.device), si.to(t.device)].cpu()  # noqa: E731
+    if "x" in inp:
+        w = inp["w"].detach().cpu()
+        if "r" in inp:
+            ry, rz, _, rdz, _ = oracle.add_rms_norm_fwd_bwd(sel(inp["x"]), sel(inp["r"]), w,
+                                                            sel(inp["gy"]), sel(inp["gz"]), eps)
+            checks = [(outs["y"], ry), (outs["z"], rz), (grads["dx"], rdz), (grads["dr"], rdz)]
+        else:
+            ry, _, rdx, _ = oracle.rms_norm_fwd_bwd(sel(inp["x"]), w, sel(inp["gy"]), eps)
+            checks = [(outs["y"], ry), (grads["dx"], rdx)]
+        for got, ref in checks:
+            note(*tolerance_ok(sel(got), ref, bf))
+    wq, wk = inp["wq"].detach().cpu(), inp["wk"].detach().cpu()
+    if "cos_q" in inp:
+        for key, H, wt in (("q", Hq, wq), ("k", Hk, wk)):
+            rsel = ((bi * S + si)[:, None] * H + torch.arange(H)[None, :]).reshape(-1)
+            rows2 = lambda t: t.detach().reshape(-1, t.shape[-1])[rsel.to(t.device)].cpu()  # noqa: E731
+            ry, _, rdx, _ = oracle.norm_rope_table_fwd_bwd(
+                rows2(inp[key]), wt, rows2(inp["cos_" + key]), rows2(inp["sin_" + key]),
+                rows2(inp["g" + key]), eps)
+            note(*tolerance_ok(rows2(outs[key + "_out"]), ry, bf))
+            note(*tolerance_ok(rows2(grads["d" + key]), rdx, bf))
+    else:
+        ref = oracle.qk_norm_rope_fwd_bwd(
+            sel(inp["q"])[None], sel(inp["k"])[None], wq, wk, sel(inp["gq"])[None],
+            sel(inp["gk"])[None], sel(inp["pos"])[None], inp["inv_freq"].cpu(), eps)
+        for key, got in (("q_out", outs["q_out"]), ("k_out", outs["k_out"]),
+                         ("dq", grads["dq"]), ("dk", grads["dk"])):
+            note(*tolerance_ok(sel(got)[None], ref[key], bf))
+
+    # ---- weight gradients summed over the ranks
+    dw_keys = [k for k in ("dw", "dwq", "dwk") if k in grads]
+    local = torch.cat([grads[k].detach().float() for k in dw_keys])
+    total, mag = local.clone(), local.abs()
+    if dist is not None:
+        dist.all_reduce(total)
+        dist.all_reduce(mag)
+    fault = bloth.device_fault()
+    rec = {"sampled_tokens_per_rank": int(flat.numel()), "sampled_worst_excess": worst}
+    # the batch rows of all ranks together: rank r holds rows r*b .. r*b+b-1
+    union = range(0, world * b)
+    if rank == 0:
+        # float64 oracle over those rows, one batch row at a time
+        ref = torch.zeros_like(total, dtype=torch.float64)
+        for r in union:
+            one = make_inputs(name, range(r, r + 1), dev, seed)
+            parts = []
+            if "x" in one:
+                w64 = one["w"].to(torch.float64)
+                if "r" in one:
+                    parts.append(oracle.add_rms_norm_fwd_bwd(one["x"], one["r"], w64, one["gy"],
+                                                             one["gz"], eps)[4])
+                else:
+                    parts.append(oracle.rms_norm_fwd_bwd(one["x"], w64, one["gy"], eps)[3])
+            if "cos_q" in one:
+                for key in ("q", "k"):
+                    parts.append(oracle.norm_rope_table_fwd_bwd(
+                        one[key].reshape(-1, D), one["w" + key].to(torch.float64),
+                        one["cos_" + key], one["sin_" + key], one["g" + key].reshape(-1, D),
+                        eps)[3])
+            else:
+                rr = oracle.qk_norm_rope_fwd_bwd(
+                    one["q"], one["k"], one["wq"].to(torch.float64),
+                    one["wk"].to(torch.float64), one["gq"], one["gk"], one["pos"],
+                    one["inv_freq"], eps)
+                parts += [rr["dwq"], rr["dwk"]]
+            ref += torch.cat(parts)
+            del one
+        bound = torch.clamp(1.6e-2 * mag.double(), min=2e-2)
+        err = (total.double() - ref).abs()
+        rec["dweight_max_abs_err_vs_oracle"] = float(err.max())
+        rec["dweight_ok_vs_oracle"] = bool((err <= bound).all())
+        ok = ok and rec["dweight_ok_vs_oracle"]
+        if world > 1:
+            full = make_inputs(name, union, dev, seed)
+            _, g1 = run_step(full, bloth)
+            one_gpu = torch.cat([g1[k].detach().float() for k in dw_keys])
+            err1 = (total.double() - one_gpu.double()).abs()
+            rec["dweight_max_abs_err_vs_one_gpu"] = float(err1.max())
+            rec["dweight_ok_vs_one_gpu"] = bool((err1 <= bound).all())
+            ok = ok and rec["dweight_ok_vs_one_gpu"]
+            del full, g1
+        rec["dweight_bound"] = "abs <= max(2e-2, 1.6e-2 * sum over ranks of |dweight_rank|)"
+    flag = torch.tensor([0.0 if ok else 1.0, float(fault)], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+    rec["ok"] = bool(flag[0].item() == 0.0)
+    rec["fault"] = int(flag[1].item())
+    return rec
 
 
 # ------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons while running."""
+    """nvidia-smi samples of SM clock and throttle reasons while running
+    (written to a temporary file that is removed afterwards)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -232,12 +410,12 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f".clocks_{os.getpid()}.csv")
+        self.path = None
 
     def __enter__(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.fh = open(self.path, "w")
+            fd, self.path = tempfile.mkstemp(prefix="bloth_clocks_", suffix=".csv")
+            self.fh = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.fh,
@@ -257,7 +435,7 @@ class ClockSampler:
             self.fh.close()
 
     def summary(self):
-        if self.proc is None or not os.path.exists(self.path):
+        if self.proc is None or self.path is None or not os.path.exists(self.path):
             return None
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -333,26 +511,19 @@ def cpu_port_step(name: str, tokens: int, seed: int = 0):
     return step
 
 
-def time_cpu(name: str, budget_s: float, steps: int | None = None, warmup: int = 1):
-    """Times the oracle port on all host cores; returns (tokens/s, sample, cores).
+def time_cpu(name: str, min_seconds: float = CPU_MIN_SECONDS, min_steps: int = 1,
+             warmup: int = 1):
+    """Times the oracle port on all host cores; returns (tokens/s, sample,
+    cores, steps).
 
-    Without `steps`, runs 512-token steps for `budget_s` seconds. With `steps`,
-    the tokens per step are scaled down (to >= 16) so that all steps take
-    about `budget_s` seconds.
-    """
+    Every step is the same fixed sample of CPU_SAMPLE_TOKENS tokens of the
+    workload; steps run until both `min_steps` steps and `min_seconds`
+    seconds are done, so the rate is averaged over at least that long."""
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    tokens = 512
+    tokens = CPU_SAMPLE_TOKENS
     step = cpu_port_step(name, tokens)
-    t0 = time.perf_counter()
-    step()
-    one = time.perf_counter() - t0
-    if steps is not None:
-        while tokens > 16 and one * steps > budget_s:
-            tokens //= 2
-            one /= 2
-        step = cpu_port_step(name, tokens)
-    for _ in range(warmup):
+    for _ in range(max(warmup, 1)):
         step()
     t0 = time.perf_counter()
     n = 0
@@ -360,12 +531,127 @@ def time_cpu(name: str, budget_s: float, steps: int | None = None, warmup: int =
         step()
         n += 1
         el = time.perf_counter() - t0
-        if (steps is not None and n >= steps) or (steps is None and el >= budget_s):
+        if n >= min_steps and el >= min_seconds:
             break
-    return tokens * n / el, f"{tokens} tokens of the workload per step, {n} steps, {el:.1f} s", cores
+    sample = (f"{tokens} tokens of the workload per step (fixed sample), {n} steps, "
+              f"{el:.1f} s, float32 oracle port on {cores} host threads")
+    return tokens * n / el, sample, cores, n
+
+
+# ------------------------------------------------------------- reference GPU
+def reference_triton_step_ms(name: str, steps: int, warmup: int) -> dict:
+    """The reference's own GPU kernels (Triton) on the same workload, one GPU:
+    ``bloth.kernels.rms_norm`` on the hidden rows and
+    ``bloth.kernels.fused_norm_rope`` on the q and k head rows, forward and
+    backward, from the reference package installed under baseline/_ref. Its
+    fused contract takes one cos/sin row per normalised row, so the tables
+    are expanded across heads (bf16, as BlothRoPE caches them) before the
+    timed region: that work is not timed, in the reference's favour. Its
+    fused backward omits the transposed rotation, so this is a speed
+    reference only. Timed like the main arm: CUDA graphs of the step. The
+    same step through this library's implementation of the same two entry
+    points, on the same inputs, is timed beside it (``same_api_b200``)."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref_dir, "bloth")):
+        return {"unavailable": "reference not installed under baseline/_ref"}
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    import bloth as ref  # noqa: F401
+    from bloth.kernels import fused_norm_rope, rms_norm
+    dev = torch.device("cuda", torch.cuda.current_device())
+    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+    inp = make_inputs(name, B, dev, seed=1234)
+    ang = inp["pos"].to(torch.float32).unsqueeze(-1) * inp["inv_freq"]  # [B, S, D/2]
+    tabs = {}
+    for key, H in (("q", Hq), ("k", Hk)):
+        c = torch.cos(ang).to(torch.bfloat16).unsqueeze(2).expand(B, S, H, D // 2)
+        s_ = torch.sin(ang).to(torch.bfloat16).unsqueeze(2).expand(B, S, H, D // 2)
+        tabs[key] = (c.reshape(-1, D // 2).contiguous(), s_.reshape(-1, D // 2).contiguous())
+
+    def step(norm, fused):
+        outs, grads, leaves = [], [], []
+        if Hd:
+            x = inp["x"].requires_grad_(True)
+            w = inp["w"].requires_grad_(True)
+            outs.append(norm(x, w, eps))
+            grads.append(inp["gy"])
+            leaves += [x, w]
+        for key, wkey, gkey in (("q", "wq", "gq"), ("k", "wk", "gk")):
+            t = inp[key].view(-1, D).requires_grad_(True)
+            w = inp[wkey].requires_grad_(True)
+            outs.append(fused(t, w, tabs[key][0], tabs[key][1], eps))
+            grads.append(inp[gkey].view(-1, D))
+            leaves += [t, w]
+        return torch.autograd.grad(outs, leaves, grads)
+
+    def time_step(norm, fused):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for _ in range(max(warmup, 3)):
+                step(norm, fused)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        unroll = next(u for u in (20, 10, 8, 5, 4, 2, 1) if steps % u == 0)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(unroll):
+                step(norm, fused)
+        replays = max(1, steps // unroll)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(replays):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize(dev)
+        del graph
+        return start.elapsed_time(end) / (replays * unroll), replays * unroll
+
+    ms_step, nsteps = time_step(rms_norm, fused_norm_rope)
+    import bloth_b200
+    ms_b200, _ = time_step(bloth_b200.rms_norm, bloth_b200.kernels.fused_norm_rope)
+    tokens = B * S
+    nbytes = step_bytes(tokens, name)["total"]
+    del inp, tabs
+    torch.cuda.empty_cache()
+    return {"ms_per_step": ms_step, "tokens_per_s": tokens / (ms_step / 1e3),
+            "steps": nsteps, "gbps": round(nbytes / (ms_step / 1e3) / 1e9, 1),
+            "workload": describe(name),
+            "note": "reference Triton kernels (rms_norm, fused_norm_rope per head row, "
+                    "per-row bf16 cos/sin tables expanded before timing), CUDA graphs",
+            "same_api_b200": {"ms_per_step": ms_b200, "tokens_per_s": tokens / (ms_b200 / 1e3),
+                              "note": "bloth_b200.rms_norm and "
+                                      "bloth_b200.kernels.fused_norm_rope on the same inputs "
+                                      "and per-row tables"}}
 
 
 # ------------------------------------------------------------- main
+def run_config(name: str, tokens_local: int, world: int, scaling: str, peak: float,
+               nbytes: dict | None = None, gbps: float | None = None) -> dict:
+    """The config object both arms print (same keys, so the lines compare)."""
+    cfg = {"workload": describe(name), "tokens_per_gpu": tokens_local, "scaling": scaling,
+           "parallelism": f"{world} independent row shard{'s' if world > 1 else ''}, "
+                          "no collective",
+           "l2": "inputs larger than L2 (each tensor >= 67 MB at 32768 tokens; at smaller "
+                 "shards the step's working set still exceeds the 126 MB L2), no flush",
+           "step_gb_per_gpu": round(step_bytes(tokens_local, name)["total"] / 1e9, 4)}
+    if gbps is not None:
+        cfg["gbps"] = round(gbps, 1)
+        cfg["frac_of_8tbs_per_gpu"] = round(gbps / world / NOMINAL_HBM_GBS, 4)
+        cfg["frac_of_measured_per_gpu"] = round(gbps / world / peak, 4)
+    return cfg
+
+
+def measured_peak() -> tuple[float, bool]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            return float(json.load(fh)["hbm_gbs"]), True
+    except (OSError, KeyError, ValueError):
+        return 6650.0, False
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -373,10 +659,19 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--workload", default="llama3-8b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference", "reference-triton"])
-    ap.add_argument("--scaling", default="weak", choices=["weak", "strong"])
+    ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
+                    help="default: strong for the sharded workloads (llama3-8b, "
+                         "qwen3-8b-packed), weak otherwise")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="on one GPU, run the shard rank 0 of an N-rank strong-scaling job "
+                         "processes")
     ap.add_argument("--e2e-steps", type=int, default=10)
-    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--cpu-seconds", type=float, default=CPU_MIN_SECONDS)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the post-run parity check (profiling runs)")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="skip timing the reference's Triton kernels beside the main line")
     ap.add_argument("--sweep", action="store_true",
                     help="bandwidth sweep over token counts 2^14..2^24 (hidden 8192 and "
                          "32q/8k heads of 128, bf16 and fp32; chunked above the resident "
@@ -391,17 +686,24 @@ def main() -> None:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     name = args.workload
     B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
+    scaling = args.scaling or default_scaling(name)
+    if args.shard_of > 1 and world > 1:
+        raise SystemExit("bench.py: --shard-of emulates one rank on one GPU; do not combine "
+                         "it with torchrun")
+    shards = max(world, args.shard_of)
+    peak, peak_measured = measured_peak()
 
     if args.impl == "reference":
         if rank != 0:
             return
-        tps, sample, cores = time_cpu(name, 90.0, steps=max(args.steps, 1),
-                                     warmup=min(max(args.warmup, 0), 3))
+        tps, sample, cores, n = time_cpu(name, args.cpu_seconds, min_steps=1,
+                                        warmup=min(max(args.warmup, 1), 3))
+        tokens_local = local_batch(B, shards, scaling) * S
         line = {"metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "impl": "reference",
-                "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+                "steps": n, "warmup": args.warmup, "impl": "reference",
+                "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic",
-                "config": {"workload": describe(name), "device": "cpu"},
+                "config": run_config(name, tokens_local, world, scaling, peak),
                 "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": cores,
                                  "kind": "port", "sample": sample},
                 "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -416,7 +718,9 @@ def main() -> None:
 
     if args.impl == "reference-triton":
         if rank == 0:
-            triton_reference(args, name)
+            torch.cuda.set_device(local)
+            rec = reference_triton_step_ms(name, args.steps, args.warmup)
+            print(json.dumps({"metric": METRIC, "impl": "reference-triton", **rec}), flush=True)
         return
 
     import bloth_b200 as bloth
@@ -433,10 +737,11 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
 
-    # tokens this rank processes per step
-    b_local = local_batch(B, world, args.scaling)
-    tokens_local = b_local * S
-    inp = make_inputs(name, b_local, dev, seed=1234 + rank, shard=(rank, world))
+    # this rank's shard of batch rows (tokens_local tokens per step)
+    rows = shard_rows(B, shards, rank, scaling)
+    tokens_local = len(rows) * S
+    seed = 1234
+    inp = make_inputs(name, rows, dev, seed=seed)
     nbytes = step_bytes(tokens_local, name)
     if args.once:
         for _ in range(args.warmup + 1):
@@ -445,6 +750,7 @@ def main() -> None:
         if dist is not None:
             dist.destroy_process_group()
         return
+    bloth.device_fault(reset=True)
 
     def barrier():
         if dist is not None:
@@ -463,6 +769,11 @@ def main() -> None:
         for _ in range(max(args.warmup, 3)):
             run_step(inp, bloth)
     torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    # kernels one step launches, counted by the library itself
+    n0 = bloth.kernel_launch_count()
+    run_step(inp, bloth)
+    launches_per_step = bloth.kernel_launch_count() - n0
     torch.cuda.synchronize(dev)
     unroll = next(u for u in (20, 10, 8, 5, 4, 2, 1) if args.steps % u == 0)  # exactly K steps
     every = 5 if unroll % 5 == 0 else 1
@@ -507,12 +818,16 @@ def main() -> None:
     # the dominant call's time per step (summed over its launches in the step:
     # the table contract calls it once for q and once for k), median over the
     # last replay's instrumented steps
-    dom_ms = sorted(sum(a.elapsed_time(b) for a, b in tm.pairs[dominant]) for tm in timers)
-    dom_ms = dom_ms[len(dom_ms) // 2]
+    dom_all = sorted(sum(a.elapsed_time(b) for a, b in tm.pairs[dominant]) for tm in timers)
+    dom_ms = dom_all[len(dom_all) // 2]
+    del graph
     ms_step = ms / steps
     tokens_total = tokens_local * world
     value = tokens_total / (ms_step / 1e3)
     gbps = nbytes["total"] * world / (ms_step / 1e3) / 1e9
+    # the fault word after the timed replays (an expired copy wait anywhere
+    # in them would show here)
+    fault_timed = int(max_over_ranks(float(bloth.device_fault()), dist, dev))
 
     # the same step called eagerly from Python (host launch overhead included)
     eager_steps = min(200, steps)
@@ -525,28 +840,22 @@ def main() -> None:
     barrier()
     eager_ms = max_over_ranks(e0.elapsed_time(e1), dist, dev) / eager_steps
 
-    # kernels launched per C-ABI call (backward entry points add the dweight
-    # reduce); the timer saw one step
-    per_step = sum(v["launches"] * (2 if k.endswith("_bwd") else 1)
-                   for k, v in per_kernel.items())
-    launches = per_step * steps
+    launches = launches_per_step * steps
     kb = {"bloth_rmsnorm_fwd": "rms_fwd", "bloth_rmsnorm_bwd": "rms_bwd",
           "bloth_add_rmsnorm_fwd": "add_fwd", "bloth_add_rmsnorm_bwd": "add_bwd",
           "bloth_qk_norm_rope_fwd": "qk_fwd", "bloth_qk_norm_rope_bwd": "qk_bwd",
           "bloth_norm_rope_fwd": "nr_fwd", "bloth_norm_rope_bwd": "nr_bwd"}
-    top = (dominant, {"mean_ms": dom_ms})
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
-            peaks = json.load(fh)
-    except OSError:
-        pass
-    peak = float(peaks.get("hbm_gbs", 6650.0))
-    top_bytes = nbytes[kb[top[0]]]
-    achieved = top_bytes / (top[1]["mean_ms"] / 1e3) / 1e9
+    top_bytes = nbytes[kb[dominant]]
+    achieved = top_bytes / (dom_ms / 1e3) / 1e9
     kernels = {k: {"launches": v["launches"], "mean_us": round(v["mean_ms"] * 1e3, 2),
                    "gbps": round(nbytes[kb[k]] / (v["total_ms"] / 1e3) / 1e9, 1)}
                for k, v in per_kernel.items()}
+    traffic = PROFILED_TRAFFIC.get((name, dominant)) if tokens_local == 32768 else None
+
+    # ---- results checked outside the timed region (every rank)
+    check = None
+    if not args.no_check:
+        check = check_step(name, inp, bloth, dev, dist, world, rank, rows, seed)
 
     # ---- end to end through the public API with host buffers
     e2e = None
@@ -555,39 +864,52 @@ def main() -> None:
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        tps, sample, cores = time_cpu(name, args.cpu_seconds)
+        tps, sample, cores, _ = time_cpu(name, args.cpu_seconds)
         cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": sample}
 
+    ref_gpu = None
+    if rank == 0 and world == 1 and args.shard_of == 1 and not args.no_reference_gpu:
+        del inp
+        torch.cuda.empty_cache()
+        try:
+            ref_gpu = reference_triton_step_ms(name, min(args.steps, 200), 3)
+        except Exception as exc:  # noqa: BLE001 - reported, never fatal to the main line
+            ref_gpu = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+
     if rank == 0:
+        cfg = run_config(name, tokens_local, world, scaling, peak, nbytes, gbps)
+        if args.shard_of > 1:
+            cfg["emulated_shard_of"] = args.shard_of
+        cfg.update({
+            "timing": f"CUDA graph of {unroll} steps through the public API, "
+                      f"{replays} replays; event pairs around the dominant call "
+                      f"in every {every}th step (roofline, median of {len(dom_all)}); the "
+                      "per-kernel breakdown below is one instrumented warm-up step",
+            "eager_ms_per_step": round(eager_ms, 4),
+            "per_gpu_tokens_per_s": round(value / world),
+            "kernels": kernels,
+            "launches_per_step": launches_per_step})
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": describe(name), "tokens_per_gpu": tokens_local,
-                       "parallelism": f"{world} independent row shards, no collective",
-                       "l2": "inputs larger than L2 (each tensor >= 67 MB at this size), no flush",
-                       "step_gb_per_gpu": round(nbytes["total"] / 1e9, 4),
-                       "gbps": round(gbps, 1),
-                       "frac_of_8tbs_per_gpu": round(gbps / world / NOMINAL_HBM_GBS, 4),
-                       "frac_of_measured_per_gpu": round(gbps / world / peak, 4),
-                       "timing": f"CUDA graph of {unroll} steps through the public API, "
-                                 f"{replays} replays; event pairs around the dominant call "
-                                 f"in every {every}th step (roofline); the per-kernel "
-                                 "breakdown below is one instrumented warm-up step",
-                       "eager_ms_per_step": round(eager_ms, 4),
-                       "kernels": kernels},
-            "roofline": {"bound": "hbm", "kernel": top[0], "achieved": round(achieved, 1),
+            "config": cfg,
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1),
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)"
-                         if "hbm_gbs" in peaks else "fallback 6650 GB/s",
-                         "traffic": PROFILED_TRAFFIC.get((name, top[0])),
+                         if peak_measured else "fallback 6650 GB/s (of fallback)",
+                         "traffic": traffic,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
-                                           "profiles/ (cold-L2 single launch)"},
+                                           "profiles/ (cold-L2 single launch at 32768 tokens)"},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
+            "fault": max(fault_timed, check["fault"] if check else 0),
+            "parity_ok": None if check is None else check["ok"],
+            "parity": check,
+            "reference_gpu": ref_gpu,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
@@ -610,13 +932,7 @@ def sweep(args) -> None:
     import bloth_b200 as bloth
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    peaks = {}
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
-            peaks = json.load(fh)
-    except OSError:
-        pass
-    peak = float(peaks.get("hbm_gbs", 6650.0))
+    peak, _ = measured_peak()
     Hd, Hq, Hk, D = 8192, 32, 8, 128
     inv = (1.0 / (5e5 ** (torch.arange(0, D // 2, dtype=torch.float32) / (D // 2)))).to(dev)
     points = []
@@ -688,98 +1004,7 @@ def sweep(args) -> None:
                     del q, k, wq, wk, gq, gk
                 torch.cuda.empty_cache()
     print(json.dumps({"sweep": "fwd+bwd bandwidth vs size, one B200", "peak_gbs": peak,
-                      "points": points}), flush=True)
-
-
-def triton_reference(args, name: str) -> None:
-    """The reference's own GPU kernels (Triton) on the same workload, one GPU:
-    ``bloth.kernels.rms_norm`` on the hidden rows and
-    ``bloth.kernels.fused_norm_rope`` on the q and k head rows, forward and
-    backward, from the reference package installed under baseline/_ref. Its
-    fused contract takes one cos/sin row per normalised row, so the tables
-    are expanded across heads (bf16, as BlothRoPE caches them) before the
-    timed region: that work is not timed, in the reference's favour. Its
-    fused backward omits the transposed rotation, so this is a speed
-    reference only. Timed like the main arm: CUDA graphs of the step."""
-    ref_dir = os.path.join(ROOT, "baseline", "_ref")
-    if not os.path.isdir(os.path.join(ref_dir, "bloth")):
-        print(json.dumps({"impl": "reference-triton",
-                          "unavailable": "reference not installed under baseline/_ref"}))
-        return
-    sys.path.insert(0, ref_dir)
-    import bloth as ref  # noqa: F401
-    from bloth.kernels import fused_norm_rope, rms_norm
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    B, S, Hd, Hq, Hk, D, theta, eps, packed = WORKLOADS[name]
-    inp = make_inputs(name, B, dev, seed=1234)
-    ang = inp["pos"].to(torch.float32).unsqueeze(-1) * inp["inv_freq"]  # [B, S, D/2]
-    tabs = {}
-    for key, H in (("q", Hq), ("k", Hk)):
-        c = torch.cos(ang).to(torch.bfloat16).unsqueeze(2).expand(B, S, H, D // 2)
-        s_ = torch.sin(ang).to(torch.bfloat16).unsqueeze(2).expand(B, S, H, D // 2)
-        tabs[key] = (c.reshape(-1, D // 2).contiguous(), s_.reshape(-1, D // 2).contiguous())
-
-    def step(norm, fused):
-        outs, grads, leaves = [], [], []
-        if Hd:
-            x = inp["x"].requires_grad_(True)
-            w = inp["w"].requires_grad_(True)
-            outs.append(norm(x, w, eps))
-            grads.append(inp["gy"])
-            leaves += [x, w]
-        for key, wkey, gkey in (("q", "wq", "gq"), ("k", "wk", "gk")):
-            t = inp[key].view(-1, D).requires_grad_(True)
-            w = inp[wkey].requires_grad_(True)
-            outs.append(fused(t, w, tabs[key][0], tabs[key][1], eps))
-            grads.append(inp[gkey].view(-1, D))
-            leaves += [t, w]
-        return torch.autograd.grad(outs, leaves, grads)
-
-    def time_step(norm, fused):
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            for _ in range(max(args.warmup, 3)):
-                step(norm, fused)
-        torch.cuda.current_stream(dev).wait_stream(side)
-        torch.cuda.synchronize(dev)
-        unroll = next(u for u in (20, 10, 8, 5, 4, 2, 1) if args.steps % u == 0)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            for _ in range(unroll):
-                step(norm, fused)
-        replays = max(1, args.steps // unroll)
-        graph.replay()
-        torch.cuda.synchronize(dev)
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        for _ in range(replays):
-            graph.replay()
-        end.record()
-        torch.cuda.synchronize(dev)
-        return start.elapsed_time(end) / (replays * unroll), replays * unroll
-
-    ms_step, steps = time_step(rms_norm, fused_norm_rope)
-    # this build behind the same reference API, on the same inputs and tables
-    import bloth_b200
-    ms_b200, _ = time_step(bloth_b200.rms_norm, bloth_b200.kernels.fused_norm_rope)
-    tokens = B * S
-    nbytes = step_bytes(tokens, name)["total"]
-    print(json.dumps({
-        "metric": METRIC, "impl": "reference-triton", "value": tokens / (ms_step / 1e3),
-        "unit": "tokens/s", "n_gpus": 1, "steps": steps, "warmup": args.warmup,
-        "ms_per_step": ms_step, "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": describe(name),
-                   "gbps": round(nbytes / (ms_step / 1e3) / 1e9, 1),
-                   "note": "reference Triton kernels (rms_norm, fused_norm_rope per row); "
-                           "cos/sin tables expanded per row before timing",
-                   "same_api_b200": {"ms_per_step": ms_b200,
-                                     "tokens_per_s": tokens / (ms_b200 / 1e3),
-                                     "note": "bloth_b200.rms_norm and "
-                                             "bloth_b200.kernels.fused_norm_rope on the same "
-                                             "inputs and per-row tables (which it reads)"}}}),
-          flush=True)
+                      "fault": bloth.device_fault(), "points": points}), flush=True)
 
 
 def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
@@ -818,7 +1043,7 @@ def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
         d.update(small)
         outs, grads = run_step(d, bloth)
         ev_free[i % 2].record(s_main)
-        res = [t.detach() for t in list(outs) + list(grads)]
+        res = [t.detach() for t in list(outs.values()) + list(grads.values())]
         if outs_host is None:
             outs_host = [torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in res]
         s_out.wait_stream(s_main)

@@ -40,8 +40,12 @@ from .modules import (  # noqa: F401
 )
 from .kernels.rope import rope_embedding  # noqa: F401
 from .patch import FastModel, patch_model  # noqa: F401
+from ._lib import BlothDeviceFault, device_fault, kernel_launch_count  # noqa: F401
 
 __all__ = [
+    "device_fault",
+    "kernel_launch_count",
+    "BlothDeviceFault",
     "kernels",
     "rms_norm",
     "BlothRMSNorm",

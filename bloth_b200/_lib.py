@@ -45,6 +45,7 @@ _SIGNATURES = {
     "bloth_last_cuda_error": (_int, []),
     "bloth_device_fault": (_int, [_int]),
     "bloth_selftest_wait_expiry": (_int, [_int, _vp]),
+    "bloth_kernel_launch_count": (_i64, []),
     "bloth_rmsnorm_fwd": (_int, [_vp, _i64, _vp, _f32, _vp, _i64, _vp, _i64, _i64, _f32, _int,
                                  _int, _vp]),
     "bloth_rmsnorm_bwd_workspace_bytes": (_sz, [_i64, _i64, _int]),
@@ -229,6 +230,52 @@ def timing_launches(external: bool = False, only=None):
         _timer = prev
 
 
+class BlothDeviceFault(RuntimeError):
+    """A kernel recorded a fault on the device (see :func:`device_fault`)."""
+
+
+def device_fault(reset: bool = False, device=None) -> int:
+    """Fault bits the library's kernels recorded on `device` (default: the
+    current CUDA device) since the last reset; 0 when every call completed.
+
+    Bit 0: a kernel gave up waiting for one of its bulk copies (after 2 s)
+    and returned early, after waiting for the copies it had already issued;
+    the results of that call are invalid. Bit 1: one of those waits gave up
+    too. Reading synchronises with the device; ``reset=True`` clears the bits.
+    The kernels never check this word themselves: read it after a step whose
+    results must be valid (or set BLOTH_CHECK_FAULTS=1 to have every call
+    check it, at the cost of a device synchronisation per call)."""
+    lib = load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else \
+        torch.device(device)
+    with torch.cuda.device(dev):
+        v = int(lib.bloth_device_fault(1 if reset else 0))
+    if v < 0:
+        raise BlothError(-v, "reading the device fault word")
+    return v
+
+
+def kernel_launch_count() -> int:
+    """Kernels this library has launched (or recorded into a capturing
+    stream) in this process."""
+    return int(load().bloth_kernel_launch_count())
+
+
+# BLOTH_CHECK_FAULTS=1: every call outside stream capture reads the device
+# fault word afterwards (a synchronisation per call) and raises on a fault.
+_CHECK_FAULTS = os.environ.get("BLOTH_CHECK_FAULTS", "") not in ("", "0")
+
+
+def _after_call(name: str, rc: int) -> int:
+    if rc == 0 and _CHECK_FAULTS and not torch.cuda.is_current_stream_capturing():
+        fault = int(load().bloth_device_fault(0))
+        if fault != 0:
+            raise BlothDeviceFault(
+                f"[Bloth] {name}: device fault word {fault:#x} (a bulk-copy wait expired; "
+                "this call's results are invalid)")
+    return rc
+
+
 def call(name: str, t: torch.Tensor, *args) -> int:
     """Calls entry point `name` with `t`'s device current (the C ABI launches
     on the calling thread's current device)."""
@@ -237,5 +284,5 @@ def call(name: str, t: torch.Tensor, *args) -> int:
         with torch.cuda.device(t.device):
             return call(name, t, *args)
     if _timer is None:
-        return fn(*args)
-    return _timer.wrap(name, t, lambda: fn(*args))
+        return _after_call(name, fn(*args))
+    return _after_call(name, _timer.wrap(name, t, lambda: fn(*args)))

@@ -23,6 +23,10 @@ namespace bloth {
 // Bit set in the device fault word when a kernel gave up waiting for a bulk
 // copy (bloth_device_fault() reads it).
 constexpr unsigned kFaultCopyTimeout = 1u;
+// Bit set when, after such an expired wait, a kernel also gave up waiting for
+// the copies it had already issued (so a copy may have still been in flight
+// when it returned).
+constexpr unsigned kFaultDrainTimeout = 2u;
 // A bulk-copy completion wait gives up after this long (the copies it waits
 // for complete in microseconds; this only bounds a broken launch).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
@@ -85,6 +89,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsign
     }
   }
   return true;
+}
+
+// After a wait on ring slot `sl` (phase `ph`) gave up: waits, each with the
+// same bound, for the `inflight` slots issued from `sl` on (sl included, the
+// ring wrapping after `nst` slots and flipping the phase), so that no bulk
+// copy this thread's CTA issued is still writing its shared memory when the
+// kernel returns. A wait that gives up here too records kFaultDrainTimeout.
+__device__ __forceinline__ void drain_ring(uint64_t* bars, int nst, int sl, uint32_t ph,
+                                           int inflight, unsigned int* fault,
+                                           unsigned long long limit_ns = kWaitLimitNs) {
+  for (int k = 0; k < inflight; ++k) {
+    if (!mbar_wait(&bars[sl], ph, nullptr, limit_ns) && fault != nullptr)
+      atomicOr(fault, kFaultDrainTimeout);
+    if (++sl == nst) {
+      sl = 0;
+      ph ^= 1u;
+    }
+  }
 }
 
 // Global -> shared bulk copy of `bytes` (multiple of 16, both addresses

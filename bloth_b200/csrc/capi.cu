@@ -10,6 +10,7 @@
 namespace bloth {
 int last_cuda_error();
 int device_fault(int reset);
+long long launch_count();
 }
 
 using namespace bloth;
@@ -165,6 +166,8 @@ const char* bloth_strerror(int status) {
 int bloth_last_cuda_error(void) { return bloth::last_cuda_error(); }
 
 int bloth_device_fault(int reset) { return bloth::device_fault(reset); }
+
+int64_t bloth_kernel_launch_count(void) { return (int64_t)bloth::launch_count(); }
 
 int bloth_selftest_wait_expiry(int limit_ms, void* stream) {
   return bloth::selftest_wait_expiry(limit_ms, as_stream(stream));

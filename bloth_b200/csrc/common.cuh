@@ -245,6 +245,11 @@ int prepare_smem(const void* func, size_t smem);
 unsigned int* fault_word();
 // Records `err` as the calling thread's last CUDA error and maps it to a status.
 int cuda_status(cudaError_t err);
+// cuda_status of a kernel launch's cudaGetLastError(), counting the launch
+// when it succeeded (bloth_kernel_launch_count).
+int launched(cudaError_t err);
+// Kernels launched by this library in this process so far.
+long long launch_count();
 // Launches the bounded-wait expiry check (bloth_selftest_wait_expiry).
 int selftest_wait_expiry(int limit_ms, cudaStream_t st);
 

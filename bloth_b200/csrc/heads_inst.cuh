@@ -26,7 +26,7 @@ int launch_head_fwd(const HeadArgs& a, cudaStream_t st) {
   if (grid < 0) return BLOTH_ERR_CUDA;
   if (grid == 0) return BLOTH_OK;
   head_pipe_kernel<T, D, MODE><<<(unsigned)grid, P::WPB * 32, P::SMEM, st>>>(a);
-  return cuda_status(cudaGetLastError());
+  return launched(cudaGetLastError());
 }
 
 template <typename T, int D>
@@ -42,7 +42,7 @@ int launch_head_bwd(const HeadArgs& a0, void* ws, size_t ws_bytes, void* dw0, vo
     HeadArgs a = a0;
     a.partials = ws;
     head_pipe_kernel<T, D, kHeadNormBwd><<<(unsigned)grid, P::WPB * 32, P::SMEM, st>>>(a);
-    const int rc = cuda_status(cudaGetLastError());
+    const int rc = launched(cudaGetLastError());
     if (rc != BLOTH_OK) return rc;
   }
   return launch_dw_reduce<AccT>(reinterpret_cast<const AccT*>(ws), grid, 2 * D, dw0, D, dw1,

@@ -405,9 +405,11 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   Cursor cc{gw, b0, s0, 0, nchunk, 0, 0};
   Cursor ic = cc;  // issue cursor, NST - 1 chunks ahead
   int isl = 0;
+  int inflight = 0;  // chunks issued and not yet computed
   for (int q = 0; q < P::NST - 1 && ic.left > 0; ++q) {
     issue(ic, isl);
     advance(ic);
+    ++inflight;
     isl = isl + 1 == P::NST ? 0 : isl + 1;
   }
 
@@ -430,6 +432,7 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
     if (ic.left > 0) {
       issue(ic, isl);
       advance(ic);
+      ++inflight;
       isl = isl + 1 == P::NST ? 0 : isl + 1;
     }
     int ten, r0, rc;
@@ -477,7 +480,13 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
       make_fwd_coef<T, D>(kc, w, cs, sn);
     }
     const bool landed = mbar_wait(&bars[csl], cph, a.fault);
-    if (!__all_sync(0xffffffffu, landed)) break;
+    if (!__all_sync(0xffffffffu, landed)) {
+      // give up the rest of the work, but not before the copies already
+      // issued into this warp's ring have landed
+      drain_ring(bars, P::NST, csl, cph, inflight, a.fault);
+      break;
+    }
+    --inflight;
     const unsigned char* slot = ring + csl * P::SLOT;
     if constexpr (BWD) {
       if (rc == P::R)

@@ -1,5 +1,6 @@
 // Launch bookkeeping shared by every entry point (SM count and occupancy
 // caches, CUDA error capture) and the deterministic weight-gradient reduce.
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <set>
@@ -17,11 +18,22 @@ __device__ unsigned int g_device_fault = 0;
 
 static thread_local int g_last_cuda_error = 0;
 
+// Kernels launched (or recorded into a capturing stream) by this library in
+// this process, over all threads and devices.
+static std::atomic<long long> g_launches{0};
+
 int cuda_status(cudaError_t err) {
   if (err == cudaSuccess) return BLOTH_OK;
   g_last_cuda_error = (int)err;
   return BLOTH_ERR_CUDA;
 }
+
+int launched(cudaError_t err) {
+  if (err == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cuda_status(err);
+}
+
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 int last_cuda_error() { return g_last_cuda_error; }
 
@@ -163,22 +175,35 @@ int launch_dw_reduce(const AccT* part, int64_t P, int N, void* dw0, int n0, void
   if (N <= 0) return BLOTH_OK;
   const unsigned grid = (unsigned)((N + 31) / 32);
   dw_reduce_kernel<AccT><<<grid, kReduceWarps * 32, 0, st>>>(part, P, N, dw0, n0, dw1, w_dt);
-  return cuda_status(cudaGetLastError());
+  return launched(cudaGetLastError());
 }
 
 template int launch_dw_reduce<float>(const float*, int64_t, int, void*, int, void*, int,
                                      cudaStream_t);
 
-// One thread waits, with the pipelines' bounded wait, on a shared-memory
-// mbarrier that nothing will ever complete (no copy is issued, nothing
-// arrives), so the wait must give up after limit_ns and record
-// kFaultCopyTimeout. Exercises the timeout path on a real GPU without any
-// fault: nothing is in flight when the kernel returns.
+// Source of the self-test's bulk copies (32 bytes, 16-byte aligned).
+__device__ __align__(16) unsigned char g_selftest_src[32];
+
+// One thread runs the pipelines' expiry path on a two-slot ring without any
+// fault. Slot 1 holds a copy issued as usual. Slot 0 expects 16 bytes whose
+// copy is not issued, so its bounded wait must give up after limit_ns and
+// record kFaultCopyTimeout. The copy of slot 0 is then issued late (as a copy
+// that lands after its wait gave up would), and the ring is drained as the
+// kernels drain it: both slots land within the limit, so kFaultDrainTimeout
+// stays clear, and nothing is in flight when the kernel returns.
 __global__ void wait_expiry_kernel(unsigned int* fault, unsigned long long limit_ns) {
-  __shared__ uint64_t bar;
-  mbar_init(&bar, 1);
+  __shared__ __align__(16) unsigned char buf[32];
+  __shared__ uint64_t bars[2];
+  mbar_init(&bars[0], 1);
+  mbar_init(&bars[1], 1);
   mbar_init_fence();
-  (void)mbar_wait(&bar, 0, fault, limit_ns);
+  mbar_arrive_expect_tx(&bars[1], 16);
+  bulk_load(buf + 16, g_selftest_src + 16, 16, &bars[1]);
+  mbar_arrive_expect_tx(&bars[0], 16);
+  if (!mbar_wait(&bars[0], 0, fault, limit_ns)) {
+    bulk_load(buf, g_selftest_src, 16, &bars[0]);
+    drain_ring(bars, 2, 0, 0, 2, fault, limit_ns);
+  }
 }
 
 int selftest_wait_expiry(int limit_ms, cudaStream_t st) {
@@ -186,7 +211,7 @@ int selftest_wait_expiry(int limit_ms, cudaStream_t st) {
   unsigned int* fault = fault_word();
   if (fault == nullptr) return cuda_status(cudaErrorInvalidDevice);
   wait_expiry_kernel<<<1, 1, 0, st>>>(fault, (unsigned long long)limit_ms * 1000000ull);
-  return cuda_status(cudaGetLastError());
+  return launched(cudaGetLastError());
 }
 template int launch_dw_reduce<double>(const double*, int64_t, int, void*, int, void*, int,
                                       cudaStream_t);

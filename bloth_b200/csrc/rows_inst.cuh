@@ -17,7 +17,7 @@ int launch_row_fwd(const RowArgs& a, cudaStream_t st) {
   const int64_t grid = need < wave ? need : wave;
   if (grid <= 0) return BLOTH_OK;
   kern<<<(unsigned)grid, BLOCK, 0, st>>>(a);
-  return cuda_status(cudaGetLastError());
+  return launched(cudaGetLastError());
 }
 
 template <typename T, int VEC, typename Cfg, int KIND>
@@ -33,7 +33,7 @@ int launch_row_bwd(const RowArgs& a0, void* ws, size_t ws_bytes, void* dw, cudaS
     auto kern = row_bwd_kernel<T, VEC, Cfg::TPR, Cfg::VPT, Cfg::RPC, KIND>;
     constexpr size_t smem = row_bwd_smem<T, VEC, Cfg>();
     kern<<<(unsigned)grid, BLOCK, smem, st>>>(a);
-    const int rc = cuda_status(cudaGetLastError());
+    const int rc = launched(cudaGetLastError());
     if (rc != BLOTH_OK) return rc;
   }
   return launch_dw_reduce<AccT>(reinterpret_cast<const AccT*>(ws), grid, a0.N, dw, a0.N, nullptr,
@@ -130,7 +130,7 @@ int launch_row_pipe_fwd(const RowArgs& a, const RowPipe& pp, cudaStream_t st) {
   if (grid == 0) return BLOTH_OK;
   row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, false>
       <<<(unsigned)grid, PC::BLOCK, pipe_smem(pp, a.N), st>>>(a, pp);
-  return cuda_status(cudaGetLastError());
+  return launched(cudaGetLastError());
 }
 
 template <typename T, int VEC, typename PC, int KIND>
@@ -146,7 +146,7 @@ int launch_row_pipe_bwd(const RowArgs& a0, const RowPipe& pp, void* ws, size_t w
     a.partials = ws;
     row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, true>
         <<<(unsigned)grid, PC::BLOCK, pipe_smem(pp, a0.N), st>>>(a, pp);
-    const int rc = cuda_status(cudaGetLastError());
+    const int rc = launched(cudaGetLastError());
     if (rc != BLOTH_OK) return rc;
   }
   return launch_dw_reduce<AccT>(reinterpret_cast<const AccT*>(ws), grid, a0.N, dw, a0.N, nullptr,

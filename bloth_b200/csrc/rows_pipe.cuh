@@ -366,7 +366,12 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
       if (i + 1 < my_blk && r2 < a.M) rstd_next = __ldg(a.rstd_in + r2);
     }
     const bool landed = mbar_wait(&bars[csl], cph, pp.fault);
-    if (!__syncthreads_and(landed)) break;
+    if (!__syncthreads_and(landed)) {
+      // give up the rest of the work, but not before the blocks already
+      // issued (this one and up to NST - 1 after it) have landed
+      drain_ring(bars, NST, csl, cph, (int)min((int64_t)NST, my_blk - i), pp.fault);
+      break;
+    }
     const unsigned char* slot = smem + (size_t)csl * pp.slot_bytes;
     if (++csl == NST) {
       csl = 0;

@@ -7,7 +7,9 @@
  * *_workspace_bytes() functions report. Every entry point is asynchronous on
  * the given stream, returns BLOTH_OK or a status code (never aborts), and
  * keeps no state between calls apart from per-device launch caches. The
- * device used is the calling thread's current CUDA device.
+ * device used is the calling thread's current CUDA device, and the stream
+ * passed must belong to that device (launch sizes, shared-memory limits and
+ * device addresses are looked up for the current device).
  *
  * Row convention (as in the reference's Triton kernels): a "row" is one
  * normalised vector of N elements; x[row, col] is at x + row*ldx + col.
@@ -65,18 +67,29 @@ const char* bloth_strerror(int status);
    this library (0 if none). */
 int bloth_last_cuda_error(void);
 
-/* Fault bits kernels recorded on the current device since the last reset
-   (bit 0: a bulk-copy completion wait gave up after its time limit and the
-   kernel returned early; its outputs are invalid). Synchronises with the
-   device; reset != 0 clears the bits. Negative on a CUDA error. */
+/* Fault bits kernels recorded on the current device since the last reset.
+   Bit 0: a bulk-copy completion wait gave up after its time limit (2 s) and
+   the kernel returned early, after waiting (with the same limit) for the
+   copies it had already issued; the outputs of that call are invalid.
+   Bit 1: one of those waits for already-issued copies gave up as well.
+   Synchronises with the device; reset != 0 clears the bits. Negative on a
+   CUDA error. The kernels never read this word: a caller that must know
+   whether a step's results are valid reads it after the step. */
 int bloth_device_fault(int reset);
-/* Diagnostic: launches one thread that waits, with the kernels' bounded
-   bulk-copy wait, on a barrier nothing completes, so the wait gives up after
-   limit_ms (1..2000) and sets fault bit 0 on the current device, as a real
-   expired copy would. Nothing is in flight when it returns, so the context
-   stays usable. Lets a deployment confirm that an expired wait ends the
+/* Diagnostic: one thread runs the kernels' expiry path on a two-slot ring
+   without any fault. One slot's copy is issued normally; the other slot
+   expects bytes whose copy is issued only after its bounded wait has given up
+   after limit_ms (1..2000), which sets fault bit 0 on the current device as a
+   real expired copy would. The ring is then drained as the kernels drain it;
+   both copies land, so bit 1 stays clear and nothing is in flight when the
+   kernel returns. Lets a deployment confirm that an expired wait ends the
    kernel and reaches bloth_device_fault(). No counterpart in the reference. */
 int bloth_selftest_wait_expiry(int limit_ms, void* stream);
+
+/* Kernels this library has launched (or recorded into a capturing stream) in
+   this process, over all threads and devices. No counterpart in the
+   reference. */
+int64_t bloth_kernel_launch_count(void);
 
 /* ------------------------------------------------------------------------
  * RMSNorm over rows of N: y = x * rsqrt(mean(x^2) + eps) * w, computed in
@@ -117,8 +130,10 @@ int bloth_rmsnorm_bwd(const void* dy, int64_t lddy, const void* x, int64_t ldx, 
    space than that (bloth_rmsnorm_bwd_workspace_bytes(M, N, dtype) >
    BLOTH_NOALLOC_SCRATCH_BYTES). Allocates nothing. The first call on each
    device sets up the array's device address (make it before any stream
-   capture). All calls share the array, so calls that overlap on the GPU race.
-   No counterpart in the reference. */
+   capture). As for every entry point, the stream must belong to the calling
+   thread's current device: the array's address and the launch size are those
+   of the current device. All calls share the array, so calls that overlap on
+   the GPU race. No counterpart in the reference. */
 int bloth_rmsnorm_bwd_noalloc(const void* dy, int64_t lddy, const void* x, int64_t ldx,
                               const void* w, float w_offset, const float* rstd, void* dx, int64_t lddx, void* dw,
                               int64_t M, int64_t N, int dtype, int w_dtype, void* stream);

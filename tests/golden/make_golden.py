@@ -6,7 +6,8 @@ compressed .npz files. Only needs the reference checkout, which exists in the
 build container (not on GPU machines); the committed .npz files are what the
 tests read.
 
-    python tests/golden/make_golden.py [/path/to/reference/bloth]
+    python tests/golden/make_golden.py /path/to/reference/bloth
+    (or BLOTH_REFERENCE=/path/to/reference/bloth python tests/golden/make_golden.py)
 
 Vectors written (all seeded):
   rmsnorm_f32.npz      reference rms_norm fwd (y, rstd) and bwd (dx, dw), fp32
@@ -30,7 +31,7 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference/bloth"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("BLOTH_REFERENCE")
 
 
 def f32(t: torch.Tensor) -> np.ndarray:
@@ -53,6 +54,9 @@ def weight(n, seed, dtype=torch.float32):
 
 
 def main() -> None:
+    if not REF or not os.path.isdir(os.path.join(REF, "bloth")):
+        raise SystemExit("make_golden.py: give the reference checkout's bloth/ directory as "
+                         "the first argument or in BLOTH_REFERENCE")
     sys.path.insert(0, REF)
     from bloth.kernels.rms_norm import rms_norm, _rms_norm_fwd_kernel, _calculate_settings
     from bloth.kernels.fused_norm_qkv_rope import (
