@@ -3,9 +3,84 @@
 #pragma once
 
 #include "heads_pipe.cuh"
+#include "qk_tok.cuh"
 #include "rows_impl.cuh"
 
 namespace bloth {
+
+// Target bytes of row data per token block (20 KB: two slots of about that
+// size per CTA, several CTAs per SM) and the slot limit beyond which the
+// per-head kernel takes the call.
+constexpr int kTokSlotTarget = 20 * 1024;
+constexpr int kTokSlotMax = 96 * 1024;
+
+// Whether the token-block kernel takes the call, and its plan: cos/sin come
+// from inv_freq; every head tensor of the call (inputs, outputs, and for the
+// backward the forward inputs) is a contiguous [B, S, H, D] tensor; for the
+// backward, each rstd run of a block is a 16-byte unit (H % 4 == 0, rstd
+// 16-byte aligned) so that it moves with the block's bulk copies.
+template <typename T, int D, bool BWD>
+bool qk_tok_plan(const HeadArgs& a, TokPlan& pl) {
+  using Q = QT<T, D, BWD>;
+  if (a.inv_freq == nullptr || a.cos != nullptr) return false;
+  const int64_t ntok = a.B * a.S;
+  const int64_t Hs[2] = {a.H[0], a.H[1]};
+  if (Hs[0] + Hs[1] < 1) return false;
+  for (int t = 0; t < 2; ++t) {
+    const int64_t H = Hs[t];
+    if (H == 0) continue;
+    auto contig = [&](const HT& h) {
+      return (H == 1 || h.sh == D) && (a.S <= 1 || h.ss == H * D) &&
+             (a.B <= 1 || h.sb == a.S * H * D);
+    };
+    if (!contig(a.src[t]) || !contig(a.dst[t]) || (BWD && !contig(a.x[t]))) return false;
+    if (BWD && (H % 4 != 0 || reinterpret_cast<uintptr_t>(a.rstd_in[t]) % 16 != 0)) return false;
+  }
+  const int hq = (int)Hs[0], hk = (int)Hs[1];
+  int tb = kTokSlotTarget / ((hq + hk) * Q::ROWB * Q::NT);
+  tb = tb < 1 ? 1 : (tb > Q::TBMAX ? Q::TBMAX : tb);
+  if (ntok < tb) tb = (int)(ntok > 0 ? ntok : 1);
+  pl.tb = tb;
+  pl.slot = Q::slot_bytes(tb, hq, hk);
+  if (pl.slot > kTokSlotMax) return false;
+  pl.nst = 2;
+  pl.s_div = FastDiv::make((uint32_t)(a.S > 0 ? a.S : 1));
+  return true;
+}
+
+// Grid of the token-block kernel: one wave of resident CTAs or fewer (-1: the
+// kernel cannot be prepared on this device).
+template <typename T, int D, bool BWD>
+int64_t qk_tok_grid(const HeadArgs& a, const TokPlan& pl) {
+  using Q = QT<T, D, BWD>;
+  auto kern = qk_token_kernel<T, D, BWD>;
+  const size_t smem = Q::smem(pl.nst, pl.slot);
+  if (prepare_smem((const void*)kern, smem) != BLOTH_OK) return -1;
+  const int occ = occupancy((const void*)kern, Q::BLOCK, smem);
+  const int64_t wave = (int64_t)device_sm_count() * (occ > 0 ? occ : 1);
+  const int64_t nblk = ceil_div(a.B * a.S, pl.tb);
+  return nblk < wave ? (nblk > 0 ? nblk : 0) : wave;
+}
+
+// Most CTAs a backward launch of the token-block kernel can have on this
+// device: a wave at the smallest shared-memory plan (an upper bound of every
+// plan's grid, for the workspace query, which does not know the head counts).
+template <typename T, int D>
+int64_t qk_tok_bwd_max_grid() {
+  using Q = QT<T, D, true>;
+  auto kern = qk_token_kernel<T, D, true>;
+  const size_t smem = Q::smem(2, 16);
+  if (prepare_smem((const void*)kern, smem) != BLOTH_OK) return -1;
+  const int occ = occupancy((const void*)kern, Q::BLOCK, smem);
+  return (int64_t)device_sm_count() * (occ > 0 ? occ : 1);
+}
+
+template <typename T, int D, bool BWD>
+int launch_qk_tok(const HeadArgs& a, const TokPlan& pl, int64_t grid, cudaStream_t st) {
+  using Q = QT<T, D, BWD>;
+  return launched(launch_pdl(qk_token_kernel<T, D, BWD>, (unsigned)grid, Q::BLOCK,
+                             Q::smem(pl.nst, pl.slot), st, a, pl));
+}
 
 // CTAs of a launch over `ntok` tokens: one wave of resident CTAs, or fewer.
 template <typename T, int D, int MODE>
@@ -22,11 +97,17 @@ int64_t head_pipe_grid(int64_t ntok) {
 template <typename T, int D, int MODE>
 int launch_head_fwd(const HeadArgs& a, cudaStream_t st) {
   using P = HP<T, D, MODE>;
+  TokPlan pl;
+  if (MODE == kHeadNormFwd && qk_tok_plan<T, D, false>(a, pl)) {
+    const int64_t grid = qk_tok_grid<T, D, false>(a, pl);
+    if (grid < 0) return BLOTH_ERR_CUDA;
+    return grid == 0 ? BLOTH_OK : launch_qk_tok<T, D, false>(a, pl, grid, st);
+  }
   const int64_t grid = head_pipe_grid<T, D, MODE>(a.B * a.S);
   if (grid < 0) return BLOTH_ERR_CUDA;
   if (grid == 0) return BLOTH_OK;
-  head_pipe_kernel<T, D, MODE><<<(unsigned)grid, P::WPB * 32, P::SMEM, st>>>(a);
-  return launched(cudaGetLastError());
+  return launched(
+      launch_pdl(head_pipe_kernel<T, D, MODE>, (unsigned)grid, P::WPB * 32, P::SMEM, st, a));
 }
 
 template <typename T, int D>
@@ -34,15 +115,23 @@ int launch_head_bwd(const HeadArgs& a0, void* ws, size_t ws_bytes, void* dw0, vo
                     cudaStream_t st) {
   using P = HP<T, D, kHeadNormBwd>;
   using AccT = typename AccOf<T>::type;
-  const int64_t grid = head_pipe_grid<T, D, kHeadNormBwd>(a0.B * a0.S);
+  TokPlan pl;
+  const bool tok = qk_tok_plan<T, D, true>(a0, pl);
+  const int64_t grid = tok ? qk_tok_grid<T, D, true>(a0, pl)
+                           : head_pipe_grid<T, D, kHeadNormBwd>(a0.B * a0.S);
   if (grid < 0) return BLOTH_ERR_CUDA;
   if ((size_t)grid * 2 * D * sizeof(AccT) > ws_bytes || (grid > 0 && ws == nullptr))
     return BLOTH_ERR_WORKSPACE;
   if (grid > 0) {
     HeadArgs a = a0;
     a.partials = ws;
-    head_pipe_kernel<T, D, kHeadNormBwd><<<(unsigned)grid, P::WPB * 32, P::SMEM, st>>>(a);
-    const int rc = launched(cudaGetLastError());
+    int rc;
+    if (tok) {
+      rc = launch_qk_tok<T, D, true>(a, pl, grid, st);
+    } else {
+      rc = launched(launch_pdl(head_pipe_kernel<T, D, kHeadNormBwd>, (unsigned)grid, P::WPB * 32,
+                               P::SMEM, st, a));
+    }
     if (rc != BLOTH_OK) return rc;
   }
   return launch_dw_reduce<AccT>(reinterpret_cast<const AccT*>(ws), grid, 2 * D, dw0, D, dw1,
@@ -87,7 +176,14 @@ size_t heads_bwd_workspace(int64_t ntok, int D) {
   size_t bytes = 0;
   dispatch_head_dim(D, [&](auto dd) {
     constexpr int DD = decltype(dd)::value;
-    const int64_t g = head_pipe_grid<T, DD, kHeadNormBwd>(ntok);
+    // the head kernel's grid, or the most CTAs the token-block kernel (which
+    // takes contiguous tensors; its grid depends on the head counts, which the
+    // query does not know) can launch
+    int64_t g = head_pipe_grid<T, DD, kHeadNormBwd>(ntok);
+    if (ntok > 0) {
+      const int64_t gt = qk_tok_bwd_max_grid<T, DD>();
+      if (gt > g) g = gt;
+    }
     bytes = (size_t)(g > 0 ? g : 0) * 2 * DD * sizeof(AccT);
   });
   return bytes;

@@ -152,10 +152,24 @@ __global__ void __launch_bounds__(kReduceWarps * 32)
   const int lane = threadIdx.x & 31;
   const int wi = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
+  pdl_wait();
+  pdl_trigger();
   double s = 0.0;
   if (col < N) {
-#pragma unroll 4
-    for (int64_t p = wi; p < P; p += kReduceWarps) s += (double)part[p * N + col];
+    // rows wi, wi + 32, ... summed in that order; their loads are issued
+    // kBatch at a time, ahead of the sums, so a column costs ceil(P / (32 *
+    // kBatch)) memory round trips instead of one per few rows
+    constexpr int kBatch = 16;
+    for (int64_t p0 = wi; p0 < P; p0 += (int64_t)kBatch * kReduceWarps) {
+      AccT v[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) {
+        const int64_t p = p0 + (int64_t)k * kReduceWarps;
+        v[k] = p < P ? part[p * N + col] : AccT(0);
+      }
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k) s += (double)v[k];
+    }
   }
   sm[wi][lane] = s;
   __syncthreads();
@@ -174,8 +188,8 @@ int launch_dw_reduce(const AccT* part, int64_t P, int N, void* dw0, int n0, void
                      cudaStream_t st) {
   if (N <= 0) return BLOTH_OK;
   const unsigned grid = (unsigned)((N + 31) / 32);
-  dw_reduce_kernel<AccT><<<grid, kReduceWarps * 32, 0, st>>>(part, P, N, dw0, n0, dw1, w_dt);
-  return launched(cudaGetLastError());
+  return launched(launch_pdl(dw_reduce_kernel<AccT>, grid, kReduceWarps * 32, 0, st, part, P, N,
+                             dw0, n0, dw1, w_dt));
 }
 
 template int launch_dw_reduce<float>(const float*, int64_t, int, void*, int, void*, int,

@@ -41,3 +41,32 @@ def test_cpu_port_runs_every_workload():
     for name in bench.WORKLOADS:
         bench.cpu_port_step(name, 16)()
     assert "fused_norm_rope" in bench.describe("llama3-8b-rows")
+
+
+def test_shards_hold_exactly_the_rows_of_the_whole_batch(monkeypatch):
+    # every batch row is seeded on its own, so the union of the ranks' shards
+    # is the unsharded batch, wherever each shard is generated (a small
+    # packed workload with the layout of the Qwen3 one)
+    cpu = torch.device("cpu")
+    name = "tiny-packed"
+    monkeypatch.setitem(bench.WORKLOADS, name, (8, 3000, 64, 4, 2, 64, 1e6, 1e-6, True))
+    B = bench.WORKLOADS[name][0]
+    full = bench.make_inputs(name, range(B), cpu)
+    for world in (2, 4, 8):
+        for rank in range(world):
+            rows = bench.shard_rows(B, world, rank, "strong")
+            part = bench.make_inputs(name, rows, cpu)
+            sl = slice(rows.start, rows.stop)
+            for key in ("x", "gy", "q", "k", "gq", "gk", "pos"):
+                assert torch.equal(part[key], full[key][sl]), (world, rank, key)
+            for key in ("w", "wq", "wk", "inv_freq"):
+                assert torch.equal(part[key], full[key])
+    # weak scaling: every rank runs a full batch of its own rows
+    assert bench.shard_rows(8, 4, 3, "weak") == range(24, 32)
+
+
+def test_sharded_workloads_default_to_strong_scaling():
+    assert bench.default_scaling("llama3-8b") == "strong"
+    assert bench.default_scaling("qwen3-8b-packed") == "strong"
+    assert bench.default_scaling("llama3.2-1b") == "weak"
+    assert bench.local_batch(8, 8, "strong") * 4096 == 4096
