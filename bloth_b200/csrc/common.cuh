@@ -232,41 +232,15 @@ __device__ __forceinline__ float group_lane_sum(float v) {
 }
 
 // ---------------------------------------------------------------------------
-// programmatic dependent launch
+// launches
 // ---------------------------------------------------------------------------
-// Every kernel of this library is launched with programmatic stream
-// serialization (launch_pdl below), so it may be scheduled while the kernel
-// before it in the stream is still finishing. pdl_wait() blocks until that
-// kernel has completed and its memory operations are visible; every kernel
-// calls it before its first global-memory access (read or write). Without a
-// programmatic predecessor it returns at once.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-// Lets the next kernel in the stream be scheduled (it still waits in its own
-// pdl_wait for this kernel to complete). Called once a CTA has consumed all
-// its inputs, so the next kernel's launch and prologue overlap this one's
-// tail.
-__device__ __forceinline__ void pdl_trigger() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
-
-// Launches kern<<<grid, block, smem, st>>>(args...) with programmatic stream
-// serialization allowed.
+// Launches kern<<<grid, block, smem, st>>>(args...) and returns the launch's
+// error (cleared, so that it does not surface at another launch).
 template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
-                       cudaStream_t st, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(block);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-  if (e != cudaSuccess) cudaGetLastError();  // leave no error behind for other launches
-  return e;
+cudaError_t launch_ex(void (*kern)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                      cudaStream_t st, Args... args) {
+  kern<<<grid, block, smem, st>>>(static_cast<KArgs>(args)...);
+  return cudaGetLastError();
 }
 
 // ---------------------------------------------------------------------------
@@ -290,5 +264,6 @@ int launched(cudaError_t err);
 long long launch_count();
 // Launches the bounded-wait expiry check (bloth_selftest_wait_expiry).
 int selftest_wait_expiry(int limit_ms, cudaStream_t st);
+
 
 }  // namespace bloth

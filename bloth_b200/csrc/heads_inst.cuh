@@ -8,11 +8,18 @@
 
 namespace bloth {
 
-// Target bytes of row data per token block (20 KB: two slots of about that
-// size per CTA, several CTAs per SM) and the slot limit beyond which the
-// per-head kernel takes the call.
-constexpr int kTokSlotTarget = 20 * 1024;
+// Target bytes of row data per token block, forward and backward, and the
+// slot limit beyond which the per-head kernel takes the call. Measured at the
+// Llama-3-8B shape (32 + 8 heads of 128, bf16), in interleaved A/B replays of
+// the whole step: backward blocks of 2 tokens (41 KB) beat 1 token by 10 us
+// per step at 32768 tokens and 1 us at 4096.
+constexpr int kTokSlotTarget[2] = {20 * 1024, 40 * 1024};
 constexpr int kTokSlotMax = 96 * 1024;
+// The forward takes the token-block kernel up to this many tokens and the
+// per-head kernel above: measured at the Llama-3-8B shape, token blocks are
+// 3.4 us per step faster at 4096 tokens and per-head warps 10 us faster at
+// 32768.
+constexpr int64_t kTokFwdMaxTokens = 8192;
 
 // Whether the token-block kernel takes the call, and its plan: cos/sin come
 // from inv_freq; every head tensor of the call (inputs, outputs, and for the
@@ -37,7 +44,8 @@ bool qk_tok_plan(const HeadArgs& a, TokPlan& pl) {
     if (BWD && (H % 4 != 0 || reinterpret_cast<uintptr_t>(a.rstd_in[t]) % 16 != 0)) return false;
   }
   const int hq = (int)Hs[0], hk = (int)Hs[1];
-  int tb = kTokSlotTarget / ((hq + hk) * Q::ROWB * Q::NT);
+  if (!BWD && ntok > kTokFwdMaxTokens) return false;
+  int tb = kTokSlotTarget[BWD ? 1 : 0] / ((hq + hk) * Q::ROWB * Q::NT);
   tb = tb < 1 ? 1 : (tb > Q::TBMAX ? Q::TBMAX : tb);
   if (ntok < tb) tb = (int)(ntok > 0 ? ntok : 1);
   pl.tb = tb;
@@ -78,8 +86,8 @@ int64_t qk_tok_bwd_max_grid() {
 template <typename T, int D, bool BWD>
 int launch_qk_tok(const HeadArgs& a, const TokPlan& pl, int64_t grid, cudaStream_t st) {
   using Q = QT<T, D, BWD>;
-  return launched(launch_pdl(qk_token_kernel<T, D, BWD>, (unsigned)grid, Q::BLOCK,
-                             Q::smem(pl.nst, pl.slot), st, a, pl));
+  return launched(launch_ex(qk_token_kernel<T, D, BWD>, (unsigned)grid, Q::BLOCK,
+                            Q::smem(pl.nst, pl.slot), st, a, pl));
 }
 
 // CTAs of a launch over `ntok` tokens: one wave of resident CTAs, or fewer.
@@ -106,8 +114,8 @@ int launch_head_fwd(const HeadArgs& a, cudaStream_t st) {
   const int64_t grid = head_pipe_grid<T, D, MODE>(a.B * a.S);
   if (grid < 0) return BLOTH_ERR_CUDA;
   if (grid == 0) return BLOTH_OK;
-  return launched(
-      launch_pdl(head_pipe_kernel<T, D, MODE>, (unsigned)grid, P::WPB * 32, P::SMEM, st, a));
+  return launched(launch_ex(head_pipe_kernel<T, D, MODE>, (unsigned)grid, P::WPB * 32, P::SMEM,
+                            st, a));
 }
 
 template <typename T, int D>
@@ -129,8 +137,8 @@ int launch_head_bwd(const HeadArgs& a0, void* ws, size_t ws_bytes, void* dw0, vo
     if (tok) {
       rc = launch_qk_tok<T, D, true>(a, pl, grid, st);
     } else {
-      rc = launched(launch_pdl(head_pipe_kernel<T, D, kHeadNormBwd>, (unsigned)grid, P::WPB * 32,
-                               P::SMEM, st, a));
+      rc = launched(launch_ex(head_pipe_kernel<T, D, kHeadNormBwd>, (unsigned)grid, P::WPB * 32,
+                              P::SMEM, st, a));
     }
     if (rc != BLOTH_OK) return rc;
   }

@@ -308,7 +308,6 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
     mbar_init_fence();
   }
   __syncwarp();
-  pdl_wait();
 
   float invf[G::APL];
 #pragma unroll
@@ -512,7 +511,6 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
       cph ^= 1u;
     }
   }
-  pdl_trigger();
 
   if constexpr (BWD) {
     // q partials are in redq; the k partials (or q's, when the warp ended in

@@ -152,8 +152,6 @@ __global__ void __launch_bounds__(kReduceWarps * 32)
   const int lane = threadIdx.x & 31;
   const int wi = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
-  pdl_wait();
-  pdl_trigger();
   double s = 0.0;
   if (col < N) {
     // rows wi, wi + 32, ... summed in that order; their loads are issued
@@ -188,8 +186,8 @@ int launch_dw_reduce(const AccT* part, int64_t P, int N, void* dw0, int n0, void
                      cudaStream_t st) {
   if (N <= 0) return BLOTH_OK;
   const unsigned grid = (unsigned)((N + 31) / 32);
-  return launched(launch_pdl(dw_reduce_kernel<AccT>, grid, kReduceWarps * 32, 0, st, part, P, N,
-                             dw0, n0, dw1, w_dt));
+  return launched(launch_ex(dw_reduce_kernel<AccT>, grid, kReduceWarps * 32, 0, st, part,
+                            P, N, dw0, n0, dw1, w_dt));
 }
 
 template int launch_dw_reduce<float>(const float*, int64_t, int, void*, int, void*, int,

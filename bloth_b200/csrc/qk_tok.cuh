@@ -177,7 +177,6 @@ __global__ void __launch_bounds__(128, BWD ? 3 : 4)
     for (int q = 0; q < nst; ++q) mbar_init(&bars[q], 1);
     mbar_init_fence();
   }
-  pdl_wait();
 
   const int Hq = a.H[0], Hk = a.H[1];
   const int ntok = (int)(a.B * a.S);  // < 2^31 / max(Hq, Hk) (host check)
@@ -447,7 +446,6 @@ __global__ void __launch_bounds__(128, BWD ? 3 : 4)
     fence_proxy_async_smem();
     __syncthreads();
   }
-  pdl_trigger();
 
   if constexpr (BWD) {
     // This CTA's partial row [q D | k D]: lanes with equal lt (the warp's row

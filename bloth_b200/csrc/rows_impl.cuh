@@ -210,7 +210,6 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_fwd_ke
   T* __restrict__ y = reinterpret_cast<T*>(a.out);
   const int N = a.N;
   const bool wv = a.w_vec != 0;
-  pdl_wait();
   int parity = 0;
   for (int64_t base = (int64_t)blockIdx.x * RPC; base < a.M;
        base += (int64_t)gridDim.x * RPC, parity ^= 1) {
@@ -264,7 +263,6 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_fwd_ke
       }
     }
   }
-  pdl_trigger();
 }
 
 __device__ __forceinline__ void acc_fma(float& acc, float a, float b) { acc = fmaf(a, b, acc); }
@@ -293,7 +291,6 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_ke
 #pragma unroll
     for (int e = 0; e < VEC; ++e) acc[j][e] = AccT(0);
 
-  pdl_wait();
   int parity = 0;
   for (int64_t base = (int64_t)blockIdx.x * RPC; base < a.M;
        base += (int64_t)gridDim.x * RPC, parity ^= 1) {
@@ -365,7 +362,6 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_ke
     }
   }
 
-  pdl_trigger();
   // Fold the RPC row groups' accumulators into group 0 in a fixed order,
   // then write this CTA's partial row.
   if constexpr (RPC > 1) {

@@ -16,7 +16,7 @@ int launch_row_fwd(const RowArgs& a, cudaStream_t st) {
   const int64_t need = ceil_div(a.M, Cfg::RPC);
   const int64_t grid = need < wave ? need : wave;
   if (grid <= 0) return BLOTH_OK;
-  return launched(launch_pdl(kern, (unsigned)grid, BLOCK, 0, st, a));
+  return launched(launch_ex(kern, (unsigned)grid, BLOCK, 0, st, a));
 }
 
 template <typename T, int VEC, typename Cfg, int KIND>
@@ -31,7 +31,7 @@ int launch_row_bwd(const RowArgs& a0, void* ws, size_t ws_bytes, void* dw, cudaS
     a.partials = ws;
     auto kern = row_bwd_kernel<T, VEC, Cfg::TPR, Cfg::VPT, Cfg::RPC, KIND>;
     constexpr size_t smem = row_bwd_smem<T, VEC, Cfg>();
-    const int rc = launched(launch_pdl(kern, (unsigned)grid, BLOCK, smem, st, a));
+    const int rc = launched(launch_ex(kern, (unsigned)grid, BLOCK, smem, st, a));
     if (rc != BLOTH_OK) return rc;
   }
   return launch_dw_reduce<AccT>(reinterpret_cast<const AccT*>(ws), grid, a0.N, dw, a0.N, nullptr,
@@ -126,8 +126,8 @@ int launch_row_pipe_fwd(const RowArgs& a, const RowPipe& pp, cudaStream_t st) {
   const int64_t grid = row_pipe_grid<T, VEC, PC, KIND, false>(a.M, a.N, pp);
   if (grid < 0) return BLOTH_ERR_CUDA;
   if (grid == 0) return BLOTH_OK;
-  return launched(launch_pdl(row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, false>,
-                             (unsigned)grid, PC::BLOCK, pipe_smem(pp, a.N), st, a, pp));
+  return launched(launch_ex(row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, false>,
+                            (unsigned)grid, PC::BLOCK, pipe_smem(pp, a.N), st, a, pp));
 }
 
 template <typename T, int VEC, typename PC, int KIND>
@@ -142,8 +142,8 @@ int launch_row_pipe_bwd(const RowArgs& a0, const RowPipe& pp, void* ws, size_t w
     RowArgs a = a0;
     a.partials = ws;
     const int rc =
-        launched(launch_pdl(row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, true>,
-                            (unsigned)grid, PC::BLOCK, pipe_smem(pp, a0.N), st, a, pp));
+        launched(launch_ex(row_pipe_kernel<T, VEC, PC::TPR, PC::VPT, PC::RPC, KIND, true>,
+                           (unsigned)grid, PC::BLOCK, pipe_smem(pp, a0.N), st, a, pp));
     if (rc != BLOTH_OK) return rc;
   }
   return launch_dw_reduce<AccT>(reinterpret_cast<const AccT*>(ws), grid, a0.N, dw, a0.N, nullptr,

@@ -242,7 +242,6 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
     for (int q = 0; q < NST; ++q) mbar_init(&bars[q], 1);
     mbar_init_fence();
   }
-  pdl_wait();
   // The thread's columns are the same for every row it processes: keep their
   // weights in registers (VPT * VEC <= 32 for every pipelined shape), and for
   // the table RoPE on narrow rows those of their rotation partners (c +- half)
@@ -604,7 +603,6 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
     fence_proxy_async_smem();
     __syncthreads();
   }
-  pdl_trigger();
 
   if constexpr (BWD) {
     // This CTA's partial dweight row: the RPC row groups' accumulators are
