@@ -314,15 +314,6 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   for (int q = 0; q < G::APL; ++q)
     invf[q] = a.inv_freq ? __ldg(a.inv_freq + lane * G::APL + q) : 0.f;
 
-  // Weights of q and k as fp32 in shared memory, shared by the CTA's warps.
-  float* wsm = reinterpret_cast<float*>(smem + P::WSM);
-  if constexpr (NORM) {
-    for (int c = threadIdx.x; c < 2 * D; c += P::WPB * 32) {
-      const int q = c / D;
-      wsm[c] = a.H[q] != 0 ? ld_any(a.w[q], c - q * D, a.w_dt) + a.w_off : 0.f;
-    }
-  }
-  __syncthreads();
 
   const int C[2] = {(a.H[0] + P::R - 1) / P::R, (a.H[1] + P::R - 1) / P::R};
   // token counts fit in 32 bits (the host rejects B*S >= 2^31)
@@ -406,12 +397,24 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   Cursor ic = cc;  // issue cursor, NST - 1 chunks ahead
   int isl = 0;
   int inflight = 0;  // chunks issued and not yet computed
+  // the first NST - 1 chunks go out before anything waits on memory, so their
+  // latency overlaps the weight loads below
   for (int q = 0; q < P::NST - 1 && ic.left > 0; ++q) {
     issue(ic, isl);
     advance(ic);
     ++inflight;
     isl = isl + 1 == P::NST ? 0 : isl + 1;
   }
+
+  // Weights of q and k as fp32 in shared memory, shared by the CTA's warps.
+  float* wsm = reinterpret_cast<float*>(smem + P::WSM);
+  if constexpr (NORM) {
+    for (int c = threadIdx.x; c < 2 * D; c += P::WPB * 32) {
+      const int q = c / D;
+      wsm[c] = a.H[q] != 0 ? ld_any(a.w[q], c - q * D, a.w_dt) + a.w_off : 0.f;
+    }
+  }
+  __syncthreads();
 
   float cs[G::VEC], sn[G::VEC];
   float snn[G::VEC];         // backward: -sin

@@ -250,14 +250,15 @@ __global__ void __launch_bounds__(128, BWD ? 3 : 4)
       w1[e] += a.w_off;
     }
   };
+  // the first NST - 1 blocks go out before anything waits on memory, so their
+  // latency overlaps the weight loads
+  for (int q = 0; q < nst - 1; ++q) issue(q, q);
   load_w(0, wq0, wq1);
   load_w(1, wk0, wk1);
 
   AccT aq0[VEC], aq1[VEC], ak0[VEC], ak1[VEC];
 #pragma unroll
   for (int e = 0; e < VEC; ++e) aq0[e] = aq1[e] = ak0[e] = ak1[e] = AccT(0);
-
-  for (int q = 0; q < nst - 1; ++q) issue(q, q);
   __syncthreads();  // barrier init visible before any wait
 
   // steps per block of each run (the same for every row group), and the row

@@ -242,39 +242,6 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
     for (int q = 0; q < NST; ++q) mbar_init(&bars[q], 1);
     mbar_init_fence();
   }
-  // The thread's columns are the same for every row it processes: keep their
-  // weights in registers (VPT * VEC <= 32 for every pipelined shape), and for
-  // the table RoPE on narrow rows those of their rotation partners (c +- half)
-  // too (wide rows load them per vector, as registers are short there).
-  constexpr bool WP_REG = ROPE && !PAIR && VPT * VEC <= 16;
-  // between the backward's two passes, rows of at most 8 values per thread
-  // keep dn and xhat in registers; the paired layout (16 values) keeps dn
-  constexpr bool KEEPX = VPT * VEC <= 8;
-  constexpr bool KEEP = KEEPX || PAIR;
-  float wr[VPT][VEC];
-  float wpr[WP_REG ? VPT : 1][VEC];
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int c = (j * TPR + lt) * VEC;
-    if (c < N) {
-      ld_weight_vec<VEC>(a, c, wv, wr[j]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < VEC; ++e) wr[j][e] = 0.f;
-    }
-    if constexpr (WP_REG) {  // signed as rope_pipe_fwd expects
-      const int64_t h = a.half;
-      if (c < 2 * h && h % VEC == 0) {
-        ld_weight_vec<VEC>(a, c < h ? c + h : c - h, wv, wpr[j]);
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) wpr[j][e] = c < h ? -wpr[j][e] : wpr[j][e];
-      } else {
-#pragma unroll
-        for (int e = 0; e < VEC; ++e) wpr[j][e] = 0.f;
-      }
-    }
-  }
-  __syncthreads();
 
   const int64_t nblk = (a.M + RPC - 1) / RPC;
   const int64_t my_blk = blockIdx.x < nblk ? (nblk - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -337,7 +304,43 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
     }
   };
 
+  // The first NST - 1 blocks go out before anything else waits on memory,
+  // so the copies' latency overlaps the weight loads below.
   for (int q = 0; q < NST - 1; ++q) issue(q, q);
+
+  // The thread's columns are the same for every row it processes: keep their
+  // weights in registers (VPT * VEC <= 32 for every pipelined shape), and for
+  // the table RoPE on narrow rows those of their rotation partners (c +- half)
+  // too (wide rows load them per vector, as registers are short there).
+  constexpr bool WP_REG = ROPE && !PAIR && VPT * VEC <= 16;
+  // between the backward's two passes, rows of at most 8 values per thread
+  // keep dn and xhat in registers; the paired layout (16 values) keeps dn
+  constexpr bool KEEPX = VPT * VEC <= 8;
+  constexpr bool KEEP = KEEPX || PAIR;
+  float wr[VPT][VEC];
+  float wpr[WP_REG ? VPT : 1][VEC];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int c = (j * TPR + lt) * VEC;
+    if (c < N) {
+      ld_weight_vec<VEC>(a, c, wv, wr[j]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) wr[j][e] = 0.f;
+    }
+    if constexpr (WP_REG) {  // signed as rope_pipe_fwd expects
+      const int64_t h = a.half;
+      if (c < 2 * h && h % VEC == 0) {
+        ld_weight_vec<VEC>(a, c < h ? c + h : c - h, wv, wpr[j]);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) wpr[j][e] = c < h ? -wpr[j][e] : wpr[j][e];
+      } else {
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) wpr[j][e] = 0.f;
+      }
+    }
+  }
+  __syncthreads();
   int isl = NST - 1;  // slot of the next block to issue
   int csl = 0;        // slot of the block being computed, and its phase
   uint32_t cph = 0;
