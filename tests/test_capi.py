@@ -207,3 +207,14 @@ def test_wait_expiry_selftest_validates_its_limit_without_gpu():
     lib = _lib.load()
     assert lib.bloth_selftest_wait_expiry(0, None) == 7
     assert lib.bloth_selftest_wait_expiry(5000, None) == 7
+
+
+def test_launch_counter_and_fault_reader_without_gpu():
+    # the launch counter is host-side: no launch has happened in this process
+    assert bloth_b200.kernel_launch_count() == 0
+    assert isinstance(bloth_b200.kernel_launch_count(), int)
+    # the fault reader needs a device; without one it raises instead of
+    # returning a stale value
+    if not torch.cuda.is_available():
+        with pytest.raises(Exception):
+            bloth_b200.device_fault()
