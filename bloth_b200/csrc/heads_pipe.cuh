@@ -295,6 +295,7 @@ __global__ void __launch_bounds__(HP<T, D, MODE>::WPB * 32, 1)
   constexpr bool BWD = MODE == kHeadNormBwd;
   constexpr bool NORM = MODE != kHeadRopeFwd;
   extern __shared__ __align__(128) unsigned char smem[];
+  if constexpr (BWD) allow_dependent_launch();  // the dweight reduce waits for this grid
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int rg = lane / G::LPR;

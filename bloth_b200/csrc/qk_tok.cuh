@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(128, BWD ? 3 : 4)
   const int grp = tid / TPR;
   const int lt = tid % TPR;
   const int nst = pl.nst, TB = pl.tb;
+  if constexpr (BWD) allow_dependent_launch();  // the dweight reduce waits for this grid
   float* cs_tab = reinterpret_cast<float*>(smem + Q::tab_off(nst, pl.slot));
   float* sn_tab = cs_tab + Q::CS_FLOATS;
   AccT* red = reinterpret_cast<AccT*>(smem + Q::red_off(nst, pl.slot));  // [WARPS][2D]

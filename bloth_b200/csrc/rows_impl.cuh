@@ -278,6 +278,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_ke
   using AccT = typename AccOf<T>::type;
   __shared__ float red[RR::SMEM_FLOATS];
   extern __shared__ __align__(16) unsigned char dsmem[];
+  allow_dependent_launch();  // the dweight reduce waits for this grid
   const int grp = threadIdx.x / TPR;
   const int lt = threadIdx.x % TPR;
   const T* __restrict__ x = reinterpret_cast<const T*>(a.x);
@@ -388,9 +389,7 @@ __global__ void __launch_bounds__(TPR* RPC, TPR * RPC <= 256 ? 2 : 1) row_bwd_ke
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const int c = (j * TPR + lt) * VEC;
-#pragma unroll
-      for (int e = 0; e < VEC; ++e)
-        if (c + e < N) part[c + e] = acc[j][e];
+      if (c < N) store_acc_vec<AccT, VEC>(part + c, acc[j], N - c);
     }
   }
 }

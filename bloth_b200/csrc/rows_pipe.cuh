@@ -237,6 +237,8 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
   const float inv_n = 1.0f / (float)N;
   const bool wv = a.w_vec != 0;
   const int NST = pp.nst;
+  // the dweight reduce that follows may launch now (it waits for this grid)
+  if constexpr (BWD) allow_dependent_launch();
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * pp.slot_bytes);
   if (threadIdx.x == 0) {
     for (int q = 0; q < NST; ++q) mbar_init(&bars[q], 1);
@@ -633,9 +635,7 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
         const int c = (j * TPR + lt) * VEC;
-#pragma unroll
-        for (int e = 0; e < VEC; ++e)
-          if (c + e < N) part[c + e] = acc[j][e];
+        if (c < N) store_acc_vec<AccT, VEC>(part + c, acc[j], N - c);
       }
     }
   }
