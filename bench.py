@@ -644,6 +644,45 @@ def run_config(name: str, tokens_local: int, world: int, scaling: str, peak: flo
     return cfg
 
 
+def stream_ceilings(dev, mib: int = 256, reps: int = 8) -> dict:
+    """Streaming rates of this GPU during the run, beside the roofline: a
+    1-read:1-write copy and a 2-read:1-write add into a third tensor (the
+    traffic mixes of the forward and the backward kernels), bf16, `mib` MiB per
+    tensor (each beyond the 126 MB L2), torch's own kernels in a CUDA graph of
+    10 operations, median of `reps` replays."""
+    n = mib * 2**20 // 2
+    x = torch.ones(n, device=dev, dtype=torch.bfloat16)
+    y = torch.ones_like(x)
+    z = torch.empty_like(x)
+    out = {"tensor_mib": mib}
+    for key, fn, moved in (("copy_1r1w_gbs", lambda: y.copy_(x), 2 * n * 2),
+                           ("add_2r1w_gbs", lambda: torch.add(x, y, out=z), 3 * n * 2)):
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(10):
+                fn()
+        g.replay()
+        times = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b) / 10)
+        times.sort()
+        out[key] = round(moved / (times[len(times) // 2] / 1e3) / 1e9, 1)
+        del g
+    del x, y, z
+    torch.cuda.empty_cache()
+    return out
+
+
 def measured_peak() -> tuple[float, bool]:
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
@@ -676,6 +715,9 @@ def main() -> None:
                     help="bandwidth sweep over token counts 2^14..2^24 (hidden 8192 and "
                          "32q/8k heads of 128, bf16 and fp32; chunked above the resident "
                          "sizes); prints one JSON line, one GPU")
+    ap.add_argument("--sweep-point", default=None,
+                    help="with --sweep, run only the points DTYPE:LG:OP (e.g. float32:16:qk; "
+                         "any field may be '*'): a fixed launch sequence for profilers")
     ap.add_argument("--once", action="store_true",
                     help="run --warmup steps and one more fwd+bwd step, untimed, and exit "
                          "(a fixed launch sequence for profilers)")
@@ -711,7 +753,7 @@ def main() -> None:
         print(json.dumps(line), flush=True)
         return
 
-    if args.sweep:
+    if args.sweep or args.sweep_point:
         if rank == 0:
             sweep(args)
         return
@@ -887,6 +929,9 @@ def main() -> None:
         except Exception as exc:  # noqa: BLE001 - reported, never fatal to the main line
             ref_gpu = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
 
+    # the GPU's own streaming rates in this run, for the roofline's context
+    ceil = stream_ceilings(dev) if rank == 0 else None
+
     if rank == 0:
         cfg = run_config(name, tokens_local, world, scaling, peak, nbytes, gbps)
         if args.shard_of > 1:
@@ -912,7 +957,14 @@ def main() -> None:
                          if peak_measured else "fallback 6650 GB/s (of fallback)",
                          "traffic": traffic,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
-                                           "profiles/ (cold-L2 single launch at 32768 tokens)"},
+                                           "profiles/ (cold-L2 single launch at 32768 tokens)",
+                         # the same call against the streaming rate of its own
+                         # traffic mix measured in this run (backward calls read
+                         # two tensors per one written, forward calls one)
+                         "stream_ceilings": ceil,
+                         "frac_of_stream_ceiling": round(
+                             achieved / ceil["add_2r1w_gbs" if dominant.endswith("_bwd")
+                                             else "copy_1r1w_gbs"], 4)},
             "cpu_baseline": cpu,
             "e2e": e2e,
             "gpu_launches": launches,
@@ -946,6 +998,14 @@ def sweep(args) -> None:
     Hd, Hq, Hk, D = 8192, 32, 8, 128
     inv = (1.0 / (5e5 ** (torch.arange(0, D // 2, dtype=torch.float32) / (D // 2)))).to(dev)
     points = []
+    want = (args.sweep_point or "*:*:*").split(":")
+    if len(want) != 3:
+        raise SystemExit("--sweep-point takes DTYPE:LG:OP")
+
+    def wanted(dt, lg, op):
+        return all(w in ("*", v) for w, v in zip(want, (str(dt).replace("torch.", ""),
+                                                        str(lg), op)))
+
     for dt, top in ((torch.bfloat16, 20), (torch.float32, 18)):
         s = torch.tensor([], dtype=dt).element_size()
         for lg in range(14, 25, 2):
@@ -953,6 +1013,8 @@ def sweep(args) -> None:
             T = (1 << lg) // nchunk
             g = torch.Generator(device=dev).manual_seed(min(lg, top))
             for op in ("hidden", "qk"):
+                if not wanted(dt, lg, op):
+                    continue
                 if op == "hidden":
                     x = torch.randn(T, Hd, generator=g, device=dev, dtype=dt).requires_grad_(True)
                     w = torch.ones(Hd, device=dev, dtype=dt).requires_grad_(True)

@@ -128,8 +128,8 @@ int launch_head_bwd(const HeadArgs& a0, void* ws, size_t ws_bytes, void* dw0, vo
   const int64_t grid = tok ? qk_tok_grid<T, D, true>(a0, pl)
                            : head_pipe_grid<T, D, kHeadNormBwd>(a0.B * a0.S);
   if (grid < 0) return BLOTH_ERR_CUDA;
-  if ((size_t)grid * 2 * D * sizeof(AccT) > ws_bytes || (grid > 0 && ws == nullptr))
-    return BLOTH_ERR_WORKSPACE;
+  const int wrc = check_workspace<AccT>(ws, (size_t)grid * 2 * D * sizeof(AccT), ws_bytes);
+  if (wrc != BLOTH_OK) return wrc;
   if (grid > 0) {
     HeadArgs a = a0;
     a.partials = ws;

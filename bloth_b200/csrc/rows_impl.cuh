@@ -461,6 +461,17 @@ int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, vo
 template <typename T>
 size_t rows_bwd_workspace(int64_t M, int N, int kind);
 
+// Checks a weight-gradient workspace for `need` bytes of AccT partial rows:
+// BLOTH_ERR_WORKSPACE when it is missing or smaller, BLOTH_ERR_ALIGN when its
+// base is not aligned to AccT (the kernels store AccT values, as 16-byte
+// vectors where the base is 16-byte aligned).
+template <typename AccT>
+inline int check_workspace(const void* ws, size_t need, size_t ws_bytes) {
+  if (need > ws_bytes || (need > 0 && ws == nullptr)) return BLOTH_ERR_WORKSPACE;
+  if (reinterpret_cast<uintptr_t>(ws) % sizeof(AccT) != 0) return BLOTH_ERR_ALIGN;
+  return BLOTH_OK;
+}
+
 // Deterministic column sum of [P][N] accumulator partials into dw (w_dt).
 template <typename AccT>
 int launch_dw_reduce(const AccT* part, int64_t P, int N, void* dw0, int n0, void* dw1, int w_dt,

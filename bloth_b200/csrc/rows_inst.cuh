@@ -24,8 +24,8 @@ int launch_row_bwd(const RowArgs& a0, void* ws, size_t ws_bytes, void* dw, cudaS
   using AccT = typename AccOf<T>::type;
   constexpr int BLOCK = Cfg::TPR * Cfg::RPC;
   const int64_t grid = row_bwd_grid<T, VEC, Cfg, KIND>(a0.M);
-  if ((size_t)grid * a0.N * sizeof(AccT) > ws_bytes || (grid > 0 && ws == nullptr))
-    return BLOTH_ERR_WORKSPACE;
+  const int wrc = check_workspace<AccT>(ws, (size_t)grid * a0.N * sizeof(AccT), ws_bytes);
+  if (wrc != BLOTH_OK) return wrc;
   if (grid > 0) {
     RowArgs a = a0;
     a.partials = ws;
@@ -136,8 +136,8 @@ int launch_row_pipe_bwd(const RowArgs& a0, const RowPipe& pp, void* ws, size_t w
   using AccT = typename AccOf<T>::type;
   const int64_t grid = row_pipe_grid<T, VEC, PC, KIND, true>(a0.M, a0.N, pp);
   if (grid < 0) return BLOTH_ERR_CUDA;
-  if ((size_t)grid * a0.N * sizeof(AccT) > ws_bytes || (grid > 0 && ws == nullptr))
-    return BLOTH_ERR_WORKSPACE;
+  const int wrc = check_workspace<AccT>(ws, (size_t)grid * a0.N * sizeof(AccT), ws_bytes);
+  if (wrc != BLOTH_OK) return wrc;
   if (grid > 0) {
     RowArgs a = a0;
     a.partials = ws;

@@ -4,7 +4,9 @@
  * Plain C: raw device pointers, element strides, an element-type code and a
  * cudaStream_t passed as void*. Nothing here allocates; the caller owns every
  * buffer, including the weight-gradient workspace whose size the
- * *_workspace_bytes() functions report. Every entry point is asynchronous on
+ * *_workspace_bytes() functions report (its base aligned to 8 bytes, or 4 for
+ * 16-bit tensors: BLOTH_ERR_ALIGN otherwise; 16-byte aligned bases are
+ * written with 16-byte stores). Every entry point is asynchronous on
  * the given stream, returns BLOTH_OK or a status code (never aborts), and
  * keeps no state between calls apart from per-device launch caches. The
  * device used is the calling thread's current CUDA device, and the stream
