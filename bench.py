@@ -754,8 +754,7 @@ def main() -> None:
         return
 
     if args.sweep or args.sweep_point:
-        if rank == 0:
-            sweep(args)
+        sweep(args, world, rank, local)
         return
 
     if args.impl == "reference-triton":
@@ -980,20 +979,27 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def sweep(args) -> None:
+def sweep(args, world: int = 1, rank: int = 0, local: int = 0) -> None:
     """fwd+bwd GB/s of the hidden RMSNorm (rows of 8192) and of the q/k pair
     (32 + 8 heads of 128, positions in-register) at token counts 2^14 .. 2^24,
     bf16 and fp32, each op alone in a CUDA graph of 10 steps. Tensors stay
-    resident up to 2^20 tokens (bf16) / 2^18 (fp32), where one op holds
-    ~40-70 GB of HBM. Larger counts (a hidden fp32 tensor at 2^24 tokens is
-    550 GB) run chunked, as rows are independent: 2^(lg - top) chunks of the
-    largest resident size through the same device buffers, in a graph of one
-    such step. Every chunk's tensors are many times the L2 size, so reusing
-    the buffers saves no traffic. Inputs ~N(0, 1); rates do not depend on
-    the values."""
+    resident up to 2^20 tokens (bf16) / 2^18 (fp32) per GPU, where one op
+    holds ~40-70 GB of HBM. Larger counts (a hidden fp32 tensor at 2^24 tokens
+    is 550 GB) run chunked, as rows are independent: chunks of the largest
+    resident size through the same device buffers, in a graph of one such
+    step. Every chunk's tensors are many times the L2 size, so reusing the
+    buffers saves no traffic. Inputs ~N(0, 1); rates do not depend on the
+    values. Under torch.distributed.run each point's tokens are split over
+    the ranks (strong scaling, no collective in the timed region); its time
+    is the max over ranks and its rate the whole job's."""
     import bloth_b200 as bloth
-    dev = torch.device("cuda", 0)
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     peak, _ = measured_peak()
     Hd, Hq, Hk, D = 8192, 32, 8, 128
     inv = (1.0 / (5e5 ** (torch.arange(0, D // 2, dtype=torch.float32) / (D // 2)))).to(dev)
@@ -1009,8 +1015,9 @@ def sweep(args) -> None:
     for dt, top in ((torch.bfloat16, 20), (torch.float32, 18)):
         s = torch.tensor([], dtype=dt).element_size()
         for lg in range(14, 25, 2):
-            nchunk = 1 << max(0, lg - top)  # chunks of the largest resident size
-            T = (1 << lg) // nchunk
+            lw = world.bit_length() - 1  # world is a power of two (1, 2, 4, 8)
+            nchunk = 1 << max(0, lg - lw - top)  # chunks of the largest resident size
+            T = (1 << lg) // world // nchunk  # tokens of one rank's chunk
             g = torch.Generator(device=dev).manual_seed(min(lg, top))
             for op in ("hidden", "qk"):
                 if not wanted(dt, lg, op):
@@ -1057,17 +1064,22 @@ def sweep(args) -> None:
                 torch.cuda.synchronize(dev)
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 reps = 3 if T >= (1 << 18) else 20
+                if dist is not None:
+                    dist.barrier()
+                    torch.cuda.synchronize(dev)
                 e0.record()
                 for _ in range(reps):
                     graph.replay()
                 e1.record()
                 torch.cuda.synchronize(dev)
-                ms = e0.elapsed_time(e1) / (unroll * reps)
+                ms = max_over_ranks(e0.elapsed_time(e1) / (unroll * reps), dist, dev)
+                nbytes *= world
                 gbps = nbytes / (ms / 1e3) / 1e9
-                total = T * nchunk
+                total = T * nchunk * world
                 points.append({"tokens": total, "dtype": str(dt).replace("torch.", ""), "op": op,
-                               "chunks": nchunk, "ms_fwd_bwd": round(ms, 4),
-                               "gbps": round(gbps, 1), "frac_of_measured": round(gbps / peak, 4),
+                               "gpus": world, "chunks": nchunk, "ms_fwd_bwd": round(ms, 4),
+                               "gbps": round(gbps, 1),
+                               "frac_of_measured_per_gpu": round(gbps / world / peak, 4),
                                "tokens_per_s": round(total / (ms / 1e3))})
                 del graph
                 if op == "hidden":
@@ -1075,8 +1087,14 @@ def sweep(args) -> None:
                 else:
                     del q, k, wq, wk, gq, gk
                 torch.cuda.empty_cache()
-    print(json.dumps({"sweep": "fwd+bwd bandwidth vs size, one B200", "peak_gbs": peak,
-                      "fault": bloth.device_fault(), "points": points}), flush=True)
+    fault = int(max_over_ranks(float(bloth.device_fault()), dist, dev))
+    if rank == 0:
+        print(json.dumps({"sweep": f"fwd+bwd bandwidth vs size, {world} B200"
+                                   f"{'s, tokens split over the ranks' if world > 1 else ''}",
+                          "peak_gbs": peak, "fault": fault, "points": points}), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def end_to_end(inp, bloth, dev, steps, barrier, dist, tokens_total):
