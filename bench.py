@@ -241,6 +241,19 @@ def make_inputs(name: str, rows, dev, seed: int = 1234):
     return inp
 
 
+def merge_summaries(sums: list) -> dict:
+    """Per-call breakdown over several instrumented steps: the call's
+    launches in one step, and the median over the steps of its time in a
+    step."""
+    out = {}
+    for name in sums[0]:
+        per_step = sorted(s[name]["total_ms"] for s in sums if name in s)
+        med = per_step[len(per_step) // 2]
+        n = sums[0][name]["launches"]
+        out[name] = {"launches": n, "total_ms": med, "mean_ms": med / n}
+    return out
+
+
 def run_step(inp, bloth):
     """One fwd+bwd pass through the public API; returns (outputs, gradients)
     as dicts keyed by name."""
@@ -832,11 +845,12 @@ def main() -> None:
         return g
 
     timers = []
-    graph_a = capture({unroll - 1})
+    n_inst = min(5, unroll)  # instrumented steps at the end of the warm-up graph
+    graph_a = capture(set(range(unroll - n_inst, unroll)))
     for _ in range(max(1, args.warmup // unroll)):
         graph_a.replay()
     barrier()
-    per_kernel = timers[0].summary()  # warm-up graph, one step
+    per_kernel = merge_summaries([tm.summary() for tm in timers])
     dominant = max(per_kernel.items(), key=lambda kv: kv[1]["total_ms"])[0]
     del graph_a
     timers = []
@@ -939,7 +953,8 @@ def main() -> None:
             "timing": f"CUDA graph of {unroll} steps through the public API, "
                       f"{replays} replays; event pairs around the dominant call "
                       f"in every {every}th step (roofline, median of {len(dom_all)}); the "
-                      "per-kernel breakdown below is one instrumented warm-up step",
+                      f"per-kernel breakdown below is the median over {n_inst} instrumented "
+                      "warm-up steps",
             "eager_ms_per_step": round(eager_ms, 4),
             "per_gpu_tokens_per_s": round(value / world),
             "kernels": kernels,

@@ -70,3 +70,11 @@ def test_sharded_workloads_default_to_strong_scaling():
     assert bench.default_scaling("qwen3-8b-packed") == "strong"
     assert bench.default_scaling("llama3.2-1b") == "weak"
     assert bench.local_batch(8, 8, "strong") * 4096 == 4096
+
+
+def test_per_kernel_breakdown_is_the_median_over_instrumented_steps():
+    steps = [{"bloth_rmsnorm_bwd": {"launches": 2, "total_ms": t, "mean_ms": t / 2}}
+             for t in (0.140, 0.131, 0.500, 0.129, 0.135)]
+    got = bench.merge_summaries(steps)["bloth_rmsnorm_bwd"]
+    assert got["launches"] == 2
+    assert got["total_ms"] == 0.135 and got["mean_ms"] == 0.135 / 2
