@@ -62,9 +62,11 @@ enum RowKind : int {
   kRowRopeVec = 3,  // kRowRope whose tables are staged in the ring and allow
                     // vector access (pipelined kernels only: neither the global
                     // table reads nor the per-element fallback are compiled)
-  kRowRopePair = 4,  // kRowRopeVec on fully rotated rows (N == 2 * half) laid out
-                     // so that a thread's second vector holds the rotation
-                     // partners of its first (TPR * VEC == half, VPT == 2)
+  kRowRopePair = 4,  // kRowRopeVec on rows rotated in full (N == 2 * half,
+                     // VPT == 2) or on their first half (N == 4 * half,
+                     // VPT == 4) laid out so that a thread's second vector
+                     // holds the rotation partners of its first
+                     // (TPR * VEC == half); vectors 2 and 3 are normalised only
 };
 
 constexpr bool row_rope(int kind) {

@@ -174,29 +174,43 @@ inline bool rows_contiguous(const RowArgs& a, int kind, bool bwd) {
 
 // Threads per row of the paired table RoPE layout for rows of 2 * half
 // (one thread per VEC columns of the first half, holding their partners of
-// the second half too), or 0 where the layout does not apply.
+// the second half too) or, for 16-bit tensors, of 4 * half (the same, plus
+// the thread's two vectors of the columns past the rotated part, as in
+// rotary embeddings on half the head dimension), or 0 where the layout does
+// not apply. Measured at 2^20 rows, fwd+bwd, against the one-vector staged
+// kernel: bf16 rows of 128 / 256 rotated on 64 / 128 columns 257 vs 450 us /
+// 495 vs 899 us; fp32 rows 540 vs 569 us / 1068 vs 975 us, so fp32 rows of
+// 4 * half keep the one-vector kernel.
 template <int V>
 constexpr int pair_tpr(int64_t N, int64_t half) {
-  if (N != 2 * half || half % V != 0) return 0;
+  if ((N != 2 * half && !(N == 4 * half && V == 8)) || half % V != 0) return 0;
   const int64_t t = half / V;
   return t == 2 || t == 4 || t == 8 || t == 16 || t == 32 ? (int)t : 0;
 }
+
+// Vectors per thread of the paired layout: 2, or 4 for rows of 4 * half.
+constexpr int pair_vpt(int64_t N, int64_t half) { return N == 4 * half ? 4 : 2; }
 
 // Calls f(RowCfg<TPR, 2, 128>{}) for the paired layout's TPR. Its pipelined
 // kernels run 128-thread CTAs: the backward (112-125 registers) then fits
 // 4 CTAs, 16 warps, per SM with half as many warps per block barrier as
 // 2 CTAs of 256 threads (measured at 2^20 rows of 128 bf16: backward 179.1 vs
 // 191.5 us, forward 129.1 us either way).
-template <typename F>
-bool dispatch_pair_cfg(int tpr, F&& f) {
+template <int VPT, typename F>
+bool dispatch_pair_tpr(int tpr, F&& f) {
   switch (tpr) {
-    case 2: f(RowCfg<2, 2, 128>{}); return true;
-    case 4: f(RowCfg<4, 2, 128>{}); return true;
-    case 8: f(RowCfg<8, 2, 128>{}); return true;
-    case 16: f(RowCfg<16, 2, 128>{}); return true;
-    case 32: f(RowCfg<32, 2, 128>{}); return true;
+    case 2: f(RowCfg<2, VPT, 128>{}); return true;
+    case 4: f(RowCfg<4, VPT, 128>{}); return true;
+    case 8: f(RowCfg<8, VPT, 128>{}); return true;
+    case 16: f(RowCfg<16, VPT, 128>{}); return true;
+    case 32: f(RowCfg<32, VPT, 128>{}); return true;
     default: return false;
   }
+}
+
+template <typename F>
+bool dispatch_pair_cfg(int tpr, int vpt, F&& f) {
+  return vpt == 4 ? dispatch_pair_tpr<4>(tpr, f) : dispatch_pair_tpr<2>(tpr, f);
 }
 
 // The pipelined kernels' table RoPE without the per-element fallback, when
@@ -225,7 +239,8 @@ int rows_fwd(const RowArgs& a, int kind, bool vec, cudaStream_t st) {
         rc = pp.nst > 0 ? launch_row_pipe_fwd<T, V, PC, K>(a, pp, st)
                         : launch_row_fwd<T, V, C, reg_kind(K)>(a, st);
       };
-      if constexpr (K == kRowRopePair) dispatch_pair_cfg(pair_tpr<V>(a.N, a.half), run);
+      if constexpr (K == kRowRopePair)
+        dispatch_pair_cfg(pair_tpr<V>(a.N, a.half), pair_vpt(a.N, a.half), run);
       else dispatch_row_cfg<V>(a.N, run);
     } else {
       dispatch_row_cfg<1>(a.N, [&](auto cfg) {
@@ -254,7 +269,8 @@ int rows_bwd(const RowArgs& a, int kind, bool vec, void* ws, size_t ws_bytes, vo
         rc = pp.nst > 0 ? launch_row_pipe_bwd<T, V, PC, K>(a, pp, ws, ws_bytes, dw, st)
                         : launch_row_bwd<T, V, C, reg_kind(K)>(a, ws, ws_bytes, dw, st);
       };
-      if constexpr (K == kRowRopePair) dispatch_pair_cfg(pair_tpr<V>(a.N, a.half), run);
+      if constexpr (K == kRowRopePair)
+        dispatch_pair_cfg(pair_tpr<V>(a.N, a.half), pair_vpt(a.N, a.half), run);
       else dispatch_row_cfg<V>(a.N, run);
     } else {
       dispatch_row_cfg<1>(a.N, [&](auto cfg) {
@@ -305,9 +321,12 @@ size_t rows_bwd_workspace(int64_t M, int N, int kind) {
   with_row_kind(kind, one_kind);
   if (kind == kRowAdd) with_row_kind(kRowNorm, one_kind);
   if (kind == kRowRope) with_row_kind(kRowRopeVec, one_kind);
-  // the paired layout of fully rotated rows (half = N / 2), and its fallback
-  if (kind == kRowRope && N % 2 == 0 && pair_tpr<V>(N, N / 2) != 0) {
-    dispatch_pair_cfg(pair_tpr<V>(N, N / 2), [&](auto cfg) {
+  // the paired layout of rows rotated in full (half = N / 2) or in half
+  // (half = N / 4), and its fallback
+  for (int parts = 2; parts <= 4; parts += 2) {
+    const int64_t h = N / parts;
+    if (kind != kRowRope || N % parts != 0 || pair_tpr<V>(N, h) == 0) continue;
+    dispatch_pair_cfg(pair_tpr<V>(N, h), pair_vpt(N, h), [&](auto cfg) {
       using C = decltype(cfg);
       using PC = PipeCfg<C::TPR, C::VPT, C::PIPE_BLOCK>;
       take(row_bwd_grid<T, V, C, kRowRope>(M));

@@ -223,7 +223,10 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
   constexpr bool ROPE = row_rope(KIND);
   // partner of a thread's vector 0 in its vector 1 (TPR * VEC == half, VPT == 2)
   constexpr bool PAIR = KIND == kRowRopePair;
-  static_assert(!PAIR || VPT == 2, "the paired layout holds a column and its partner");
+  // the paired layout holds a column and its rotation partner (vectors 0 and
+  // 1); rows of 4 * half add the two vectors of the columns past the rotated
+  // part, which are normalised only
+  static_assert(!PAIR || VPT == 2 || VPT == 4, "paired rows are 2 or 4 halves wide");
   constexpr bool CSV = KIND == kRowRopeVec || PAIR;  // staged tables, vector access
   constexpr bool RES = KIND == kRowAdd;
   constexpr int NTEN = row_pipe_inputs(KIND, BWD);
@@ -457,6 +460,18 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
           }
           stg_pack_stream<T, VEC>(yr + c0, pack<T, VEC>(f0));
           stg_pack_stream<T, VEC>(yr + c0 + TPR * VEC, pack<T, VEC>(f1));
+#pragma unroll
+          for (int j = 2; j < VPT; ++j) {  // columns past the rotated part
+            float f[VEC];
+            unpack(xp[j], f);
+#pragma unroll
+            for (int e = 0; e < VEC; e += 2) {
+              const float2 y = f2_mul(f2_mul(f2(f[e], f[e + 1]), r2), f2(wr[j][e], wr[j][e + 1]));
+              f[e] = y.x;
+              f[e + 1] = y.y;
+            }
+            stg_pack_stream<T, VEC>(yr + (j * TPR + lt) * VEC, pack<T, VEC>(f));
+          }
         } else {
 #pragma unroll
         for (int j = 0; j < VPT; ++j) {
@@ -521,10 +536,10 @@ __global__ void __launch_bounds__(TPR* RPC, row_pipe_min_ctas(TPR * RPC, VPT, KI
         const int c = (j * TPR + lt) * VEC;
         if (valid && c < N) {
           float xf[VEC], dn[VEC];
-          if constexpr (PAIR) {
+          if (PAIR && j < 2) {  // rotated: R^T dy from above
 #pragma unroll
-            for (int e = 0; e < VEC; ++e) dn[e] = dpr[PAIR ? j : 0][e];
-          } else {
+            for (int e = 0; e < VEC; ++e) dn[e] = dpr[PAIR && j < 2 ? j : 0][e];
+          } else {  // (paired rows: columns past the rotated part take dy as it is)
             unpack(lds_pack<T, VEC>(dyp + (int64_t)c * sizeof(T)), dn);
           }
           unpack(lds_pack<T, VEC>(xrp + (int64_t)c * sizeof(T)), xf);

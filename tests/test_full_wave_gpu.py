@@ -10,9 +10,10 @@ up to 32 rows each) through the library's own workspace query and check the
 results against the oracle, evaluated in float64 on the GPU. The table cases
 cover cos/sin rows that are staged in one copy per block (contiguous), one
 copy per row (strided, 16-byte aligned) and read from global memory
-(strided, misaligned). Staged tables on fully rotated rows take the paired
-layout (a thread holds a column and its rotation partner), with 2 to 32
-threads per row over these widths. Tolerances are the path's (see
+(strided, misaligned). Staged tables on fully rotated rows, and on 16-bit
+rows rotated on their first half, take the paired layout (a thread holds a
+column and its rotation partner), with 2 to 32 threads per row over these
+widths. Tolerances are the path's (see
 oracle.tolerance_ok).
 """
 import pytest
@@ -54,6 +55,33 @@ def test_table_rope_backward_full_wave(cuda, dtype, N, layout):
     if layout == "contiguous":
         cos, sin = cos.contiguous(), sin.contiguous()
     assert cos.stride(0) == h + pad
+    y, rstd = norm_rope_forward(x, w, cos, sin, eps)
+    dx, dw = norm_rope_backward(dy, x, w, cos, sin, rstd)
+    torch.cuda.synchronize()
+    ry, _, rdx, rdw = oracle.norm_rope_table_fwd_bwd(x, w, cos, sin, dy, eps)
+    _check(y, ry, dtype, f"{layout} y")
+    _check(dx, rdx, dtype, f"{layout} dx")
+    _check(dw, rdw, dtype, f"{layout} dw", oracle.norm_rope_table_dw_scale(x, cos, sin, dy, eps))
+    assert bloth_b200._lib.load().bloth_device_fault(0) == 0
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("N", [128, 256, 512])
+@pytest.mark.parametrize("layout", ["contiguous", "strided"])
+def test_half_rotated_table_rope_backward_full_wave(cuda, dtype, N, layout):
+    # rotation on the first half of each row (half = N / 4; the paired layout
+    # with two more vectors per thread when the tables are staged)
+    M, h, eps = _rows(N), N // 4, 1e-6
+    x = seeded_normal((M, N), dtype, 5).to(cuda)
+    w = seeded_weight(N, dtype, 6).to(cuda)
+    dy = seeded_normal((M, N), dtype, 7).to(cuda)
+    pad = {"contiguous": 0, "strided": 8}[layout]
+    ang = seeded_normal((M, h + pad), torch.float32, 8).to(cuda) * 3.0
+    cs_dtype = torch.float32 if dtype == torch.float32 else dtype
+    cos = ang.cos().to(cs_dtype)[:, :h]
+    sin = ang.sin().to(cs_dtype)[:, :h]
+    if layout == "contiguous":
+        cos, sin = cos.contiguous(), sin.contiguous()
     y, rstd = norm_rope_forward(x, w, cos, sin, eps)
     dx, dw = norm_rope_backward(dy, x, w, cos, sin, rstd)
     torch.cuda.synchronize()

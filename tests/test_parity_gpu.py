@@ -437,13 +437,16 @@ def test_table_variant_edge_cases(cuda):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("N", [32, 64, 128, 256])
-def test_paired_table_rows_with_strided_inputs(cuda, dtype, N):
-    # Fully rotated rows with staged tables take the paired layout (a thread
-    # holds a column and its rotation partner), 4-64 rows per block at these
-    # widths. Strided x and dy rows are bulk-copied one row at a time, and
-    # 1001 rows leave a partial last block. The weight is applied as w + 1.
+@pytest.mark.parametrize("parts", [2, 4])
+def test_paired_table_rows_with_strided_inputs(cuda, dtype, N, parts):
+    # Rows rotated in full (half = N/2) or on their first half (half = N/4,
+    # the other half normalised only) with staged tables take the paired
+    # layout (a thread holds a column and its rotation partner, and for
+    # half = N/4 two vectors past the rotated part), 4-64 rows per block at
+    # these widths. Strided x and dy rows are bulk-copied one row at a time,
+    # and 1001 rows leave a partial last block. The weight is applied as w + 1.
     from bloth_b200.kernels.fused_norm_qkv_rope import norm_rope_backward, norm_rope_forward
-    M, h, eps, off = 1001, N // 2, 1e-6, 1.0
+    M, h, eps, off = 1001, N // parts, 1e-6, 1.0
     x = seeded_normal((M, N + 8), dtype, 40).to(cuda)[:, :N]
     dy = seeded_normal((M, N + 8), dtype, 41).to(cuda)[:, :N]
     w = (seeded_weight(N, torch.float32, 42) - 1.0).to(dtype).to(cuda)
